@@ -1,0 +1,59 @@
+// Device-side forest and the kernel launchers (internal to csrc/cuda).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace mlk::cuda {
+
+// Everything a kernel needs, passed by value as a kernel parameter.
+struct ForestArgs {
+    int F, K, T, slots, pad_slot;
+    int le, cast_f32, mean, link;
+    double sigmoid_scale;
+    int standardize, clip;
+    double lo, hi;
+    const double* pre_mean;
+    const double* pre_scale;
+    const int4* nodes;          // [nodes]: T, slot, left, right
+    const double* leaf_value;   // [nodes]
+    const int* roots;           // [T]
+    const int* depth;           // [T]
+    const int* tree_output;     // [T]
+    const int4* slot_of;        // [F]: slot per variant, -1 when unused
+    const double* base;         // [K]
+    const int* counts;          // [K]
+    const double* threshold;    // [nodes]
+    const int* feature;         // [nodes]
+    // Complete-tree view (complete_depth > 0).
+    int complete_depth;
+    const int2* heap_words;     // [T * (2^d - 1)]: T, slot
+    const double* heap_leaf;    // [T * 2^d]
+    const int* heap_leaf_id;    // [T * 2^d]
+};
+
+struct DevForest {
+    int device = 0;
+    int sm_count = 0;
+    ForestArgs args{};
+    void* blocks[20] = {};  // device allocations, freed with the forest
+    int nblocks = 0;
+};
+
+// Queues one predict (out != nullptr) or leaf-index (leaves != nullptr) pass
+// over device buffers on `stream`. `scratch` holds scratch_bytes(f) bytes of
+// device memory (nullptr when that is 0). Returns false with `err` set.
+bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
+                   cudaStream_t stream, std::string& err, int* scratch);
+
+// Device scratch a launch needs: 0 unless the key table of a warp exceeds
+// shared memory (models with thousands of features), when the tables live in
+// global memory, one per resident warp.
+size_t scratch_bytes(const DevForest& f);
+
+// One-time per-device kernel attributes (dynamic shared memory limits).
+bool prepare_kernels(const DevForest& f, std::string& err);
+
+}  // namespace mlk::cuda

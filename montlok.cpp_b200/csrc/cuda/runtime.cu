@@ -1,0 +1,488 @@
+// Host side of the CUDA layer: device replicas of a forest, per-thread
+// workspaces (streams, device buffers, pinned staging) and the pipelined
+// host-buffer predict behind montlok_model_predict.
+//
+// Host-buffer calls split the rows into chunks and alternate two streams:
+// while one chunk's kernel runs, the next chunk's input is copied host ->
+// device on the other stream (straight from the caller's memory when it is
+// pinned, else through a pinned staging buffer) and the previous chunk's
+// results come back device -> host. Each calling thread has its own
+// workspace per device, so concurrent calls on one model never share
+// buffers.
+//
+// MONTLOK_FAULT_INJECT=alloc|copy|launch makes the next device allocation,
+// copy or launch of a call fail as if CUDA had failed; tests use it to check
+// that failures surface as MONTLOK_ERROR_INTERNAL with a message.
+#include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "forest.cuh"
+#include "mlk_cuda.h"
+
+namespace mlk::cuda {
+namespace {
+
+constexpr int kInternal = 7;
+constexpr int kInvalid = 1;
+constexpr size_t kChunkBytes = size_t{64} << 20;  // input bytes per pipelined chunk
+
+std::atomic<int> g_copy_threads{1};
+
+void put_error(char* err, size_t errlen, const std::string& message) {
+    if (!err || errlen == 0) return;
+    const size_t n = std::min(errlen - 1, message.size());
+    std::memcpy(err, message.data(), n);
+    err[n] = '\0';
+}
+
+bool injected(const char* what) {
+    const char* v = std::getenv("MONTLOK_FAULT_INJECT");
+    return v && std::strcmp(v, what) == 0;
+}
+
+bool ok(cudaError_t e, const char* what, std::string& err) {
+    if (e == cudaSuccess) return true;
+    err = std::string(what) + " failed: " + cudaGetErrorString(e);
+    cudaGetLastError();
+    return false;
+}
+
+// Restores the calling thread's current device on scope exit.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&previous_) != cudaSuccess) previous_ = -1;
+        if (previous_ != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (previous_ >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous_) cudaSetDevice(previous_);
+    }
+
+private:
+    int previous_ = -1;
+};
+
+bool device_alloc(void** p, size_t bytes, std::string& err) {
+    if (injected("alloc")) {
+        err = "cudaMalloc failed: injected fault (MONTLOK_FAULT_INJECT=alloc)";
+        return false;
+    }
+    return ok(cudaMalloc(p, bytes), "cudaMalloc", err);
+}
+
+bool host_alloc(void** p, size_t bytes, std::string& err) {
+    if (injected("alloc")) {
+        err = "cudaMallocHost failed: injected fault (MONTLOK_FAULT_INJECT=alloc)";
+        return false;
+    }
+    return ok(cudaMallocHost(p, bytes), "cudaMallocHost", err);
+}
+
+bool copy_async(void* dst, const void* src, size_t bytes, cudaMemcpyKind kind, cudaStream_t s, std::string& err) {
+    if (bytes == 0) return true;
+    if (injected("copy")) {
+        err = "cudaMemcpyAsync failed: injected fault (MONTLOK_FAULT_INJECT=copy)";
+        return false;
+    }
+    return ok(cudaMemcpyAsync(dst, src, bytes, kind, s), "cudaMemcpyAsync", err);
+}
+
+// memcpy split over the library's worker threads for large blocks.
+void host_copy(void* dst, const void* src, size_t bytes) {
+    const int threads = std::max(1, g_copy_threads.load(std::memory_order_relaxed));
+    constexpr size_t kPerThread = size_t{4} << 20;
+    const size_t parts = std::min<size_t>(static_cast<size_t>(threads), std::max<size_t>(1, bytes / kPerThread));
+    if (parts <= 1) {
+        std::memcpy(dst, src, bytes);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const size_t step = (bytes + parts - 1) / parts;
+    for (size_t i = 1; i < parts; ++i) {
+        const size_t lo = i * step, hi = std::min(bytes, lo + step);
+        if (lo < hi) {
+            pool.emplace_back([=] {
+                std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
+            });
+        }
+    }
+    std::memcpy(dst, src, std::min(bytes, step));
+    for (auto& t : pool) t.join();
+}
+
+// A device buffer that only grows.
+struct DeviceBuffer {
+    void* p = nullptr;
+    size_t cap = 0;
+    bool reserve(size_t bytes, std::string& err) {
+        if (bytes <= cap) return true;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        if (!device_alloc(&p, bytes, err)) return false;
+        cap = bytes;
+        return true;
+    }
+    ~DeviceBuffer() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct PinnedBuffer {
+    void* p = nullptr;
+    size_t cap = 0;
+    bool reserve(size_t bytes, std::string& err) {
+        if (bytes <= cap) return true;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        if (!host_alloc(&p, bytes, err)) return false;
+        cap = bytes;
+        return true;
+    }
+    ~PinnedBuffer() {
+        if (p) cudaFreeHost(p);
+    }
+};
+
+struct Workspace {
+    cudaStream_t stream[2] = {nullptr, nullptr};
+    DeviceBuffer dx[2], dout[2], scratch;
+    PinnedBuffer hx[2], hout[2];
+    ~Workspace() {
+        for (auto s : stream) {
+            if (s) cudaStreamDestroy(s);
+        }
+    }
+};
+
+Workspace* workspace(int device, std::string& err) {
+    thread_local std::map<int, std::unique_ptr<Workspace>> spaces;
+    auto& w = spaces[device];
+    if (!w) {
+        auto fresh = std::make_unique<Workspace>();
+        for (auto& s : fresh->stream) {
+            if (!ok(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate", err)) return nullptr;
+        }
+        w = std::move(fresh);
+    }
+    return w.get();
+}
+
+// A pending chunk whose results sit in a pinned staging buffer.
+struct Pending {
+    bool live = false;
+    size_t bytes = 0;
+    void* dst = nullptr;
+};
+
+template <typename Out>
+int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* out, size_t out_per_row, bool leaves,
+             char* err, size_t errlen) {
+    std::string e;
+    DeviceGuard guard(f.device);
+    Workspace* w = workspace(f.device, e);
+    if (!w) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    const size_t elem = dtype == 1 ? 4 : 8;
+    const size_t row_in = static_cast<size_t>(f.args.F) * elem;
+    const size_t row_out = out_per_row * sizeof(Out);
+    size_t chunk = std::max<size_t>(1024, kChunkBytes / std::max<size_t>(row_in, 1));
+    chunk = std::min(chunk, batch);
+
+    int kx = MLK_PTR_PAGEABLE, ko = MLK_PTR_PAGEABLE, dev = -1;
+    mlk_cuda_pointer_kind(x, &kx, &dev);
+    mlk_cuda_pointer_kind(out, &ko, &dev);
+    const bool pin_x = kx == MLK_PTR_PINNED, pin_out = ko == MLK_PTR_PINNED;
+    const bool dev_x = kx == MLK_PTR_DEVICE, dev_out = ko == MLK_PTR_DEVICE;
+
+    const size_t scratch = scratch_bytes(f);
+    if (scratch && !w->scratch.reserve(scratch, e)) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    for (int s = 0; s < 2; ++s) {
+        if ((!dev_x && !w->dx[s].reserve(chunk * row_in, e)) || (!dev_out && !w->dout[s].reserve(chunk * row_out, e)) ||
+            (!dev_x && !pin_x && !w->hx[s].reserve(chunk * row_in, e)) ||
+            (!dev_out && !pin_out && !w->hout[s].reserve(chunk * row_out, e))) {
+            put_error(err, errlen, e);
+            return kInternal;
+        }
+    }
+    Pending pending[2];
+    auto drain = [&](int s) -> bool {
+        if (!pending[s].live) return true;
+        if (!ok(cudaStreamSynchronize(w->stream[s]), "cudaStreamSynchronize", e)) return false;
+        std::memcpy(pending[s].dst, w->hout[s].p, pending[s].bytes);
+        pending[s].live = false;
+        return true;
+    };
+    bool good = true;
+    size_t c = 0;
+    for (size_t r0 = 0; r0 < batch && good; r0 += chunk, ++c) {
+        const int s = static_cast<int>(c & 1);
+        const size_t rows = std::min(chunk, batch - r0);
+        cudaStream_t st = w->stream[s];
+        // The staging buffers of stream s are reused: wait for its last chunk.
+        if (pending[s].live) {
+            good = drain(s);
+        } else if (c >= 2 && !pin_x && !dev_x) {
+            good = ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
+        }
+        if (!good) break;
+        const char* src = static_cast<const char*>(x) + r0 * row_in;
+        const void* dsrc = src;
+        if (!dev_x) {
+            if (!pin_x) {
+                host_copy(w->hx[s].p, src, rows * row_in);
+                src = static_cast<const char*>(w->hx[s].p);
+            }
+            good = copy_async(w->dx[s].p, src, rows * row_in, cudaMemcpyHostToDevice, st, e);
+            dsrc = w->dx[s].p;
+        }
+        if (!good) break;
+        void* dst_dev = dev_out ? static_cast<void*>(out + r0 * out_per_row) : w->dout[s].p;
+        if (injected("launch")) {
+            e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
+            good = false;
+            break;
+        }
+        good = launch_forest(f, dtype, dsrc, static_cast<long long>(rows), leaves ? nullptr : static_cast<double*>(dst_dev),
+                             leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, static_cast<int*>(w->scratch.p));
+        if (!good) break;
+        if (!dev_out) {
+            if (pin_out) {
+                good = copy_async(out + r0 * out_per_row, dst_dev, rows * row_out, cudaMemcpyDeviceToHost, st, e);
+            } else {
+                good = copy_async(w->hout[s].p, dst_dev, rows * row_out, cudaMemcpyDeviceToHost, st, e);
+                pending[s] = Pending{true, rows * row_out, out + r0 * out_per_row};
+            }
+        }
+    }
+    for (int s = 0; s < 2; ++s) {
+        if (good) good = drain(s);
+        if (good) good = ok(cudaStreamSynchronize(w->stream[s]), "cudaStreamSynchronize", e);
+        else cudaStreamSynchronize(w->stream[s]);
+    }
+    if (!good) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    return 0;
+}
+
+}  // namespace
+}  // namespace mlk::cuda
+
+struct mlk_dev_forest {
+    mlk::cuda::DevForest f;
+};
+
+using mlk::cuda::DevForest;
+using mlk::cuda::put_error;
+
+extern "C" {
+
+void mlk_cuda_set_copy_threads(int threads) { mlk::cuda::g_copy_threads.store(std::max(1, threads)); }
+
+int mlk_cuda_device_count(int* count, char* err, size_t errlen) {
+    *count = 0;
+    const cudaError_t e = cudaGetDeviceCount(count);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *count = 0;
+        put_error(err, errlen, std::string("no CUDA device is available: ") + cudaGetErrorString(e));
+        return mlk::cuda::kInternal;
+    }
+    if (*count == 0) {
+        put_error(err, errlen, "no CUDA device is available");
+        return mlk::cuda::kInternal;
+    }
+    return 0;
+}
+
+int mlk_cuda_current_device(int* device, char* err, size_t errlen) {
+    const cudaError_t e = cudaGetDevice(device);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        put_error(err, errlen, std::string("cudaGetDevice failed: ") + cudaGetErrorString(e));
+        return mlk::cuda::kInternal;
+    }
+    return 0;
+}
+
+int mlk_cuda_pointer_kind(const void* p, int* kind, int* device) {
+    *kind = MLK_PTR_PAGEABLE;
+    if (device) *device = -1;
+    cudaPointerAttributes attr{};
+    if (!p || cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        *kind = MLK_PTR_DEVICE;
+        if (device) *device = attr.device;
+    } else if (attr.type == cudaMemoryTypeHost) {
+        *kind = MLK_PTR_PINNED;
+    }
+    return 0;
+}
+
+int mlk_cuda_forest_device(const mlk_dev_forest* forest) { return forest->f.device; }
+
+int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest** out, char* err, size_t errlen) {
+    using namespace mlk::cuda;
+    *out = nullptr;
+    std::string e;
+    DeviceGuard guard(device);
+    auto holder = std::make_unique<mlk_dev_forest>();
+    DevForest& f = holder->f;
+    f.device = device;
+    if (!ok(cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute", e)) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    // One allocation; every array 256-byte aligned inside it.
+    struct Part {
+        const void* src;
+        size_t bytes;
+        size_t at;
+    };
+    std::vector<Part> parts;
+    size_t total = 0;
+    auto add = [&](const void* src, size_t bytes) {
+        parts.push_back(Part{src, bytes, total});
+        total += (bytes + 255) & ~size_t{255};
+        return parts.size() - 1;
+    };
+    const size_t n = static_cast<size_t>(v->nodes), T = static_cast<size_t>(v->trees);
+    const size_t F = static_cast<size_t>(v->features), K = static_cast<size_t>(v->outputs);
+    const size_t i_nodes = add(v->node_words, n * 16), i_leaf = add(v->leaf_value, n * 8);
+    const size_t i_roots = add(v->roots, T * 4), i_depth = add(v->depth, T * 4), i_out = add(v->tree_output, T * 4);
+    const size_t i_slot = add(v->slot_of, F * 16), i_base = add(v->base, K * 8), i_counts = add(v->counts, K * 4);
+    const size_t i_thr = add(v->threshold, n * 8), i_feat = add(v->feature, n * 4);
+    const size_t i_mean = v->standardize ? add(v->pre_mean, F * 8) : SIZE_MAX;
+    const size_t i_scale = v->standardize ? add(v->pre_scale, F * 8) : SIZE_MAX;
+    std::vector<unsigned char> staging(total, 0);
+    for (const Part& p : parts) {
+        if (p.bytes) std::memcpy(staging.data() + p.at, p.src, p.bytes);
+    }
+    void* block = nullptr;
+    if (!device_alloc(&block, std::max<size_t>(total, 256), e) ||
+        !ok(cudaMemcpy(block, staging.data(), total, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
+        if (block) cudaFree(block);
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    f.blocks[f.nblocks++] = block;
+    auto at = [&](size_t i) { return static_cast<unsigned char*>(block) + parts[i].at; };
+    ForestArgs& a = f.args;
+    a.F = v->features;
+    a.K = v->outputs;
+    a.T = v->trees;
+    a.slots = v->slots;
+    a.pad_slot = v->pad_slot;
+    a.le = v->decision_le;
+    a.cast_f32 = v->cast_f32;
+    a.mean = v->mean;
+    a.link = v->link;
+    a.sigmoid_scale = v->sigmoid_scale;
+    a.standardize = v->standardize;
+    a.clip = v->clip;
+    a.lo = v->clip_lo;
+    a.hi = v->clip_hi;
+    a.pre_mean = v->standardize ? reinterpret_cast<const double*>(at(i_mean)) : nullptr;
+    a.pre_scale = v->standardize ? reinterpret_cast<const double*>(at(i_scale)) : nullptr;
+    a.nodes = reinterpret_cast<const int4*>(at(i_nodes));
+    a.leaf_value = reinterpret_cast<const double*>(at(i_leaf));
+    a.roots = reinterpret_cast<const int*>(at(i_roots));
+    a.depth = reinterpret_cast<const int*>(at(i_depth));
+    a.tree_output = reinterpret_cast<const int*>(at(i_out));
+    a.slot_of = reinterpret_cast<const int4*>(at(i_slot));
+    a.base = reinterpret_cast<const double*>(at(i_base));
+    a.counts = reinterpret_cast<const int*>(at(i_counts));
+    a.threshold = reinterpret_cast<const double*>(at(i_thr));
+    a.feature = reinterpret_cast<const int*>(at(i_feat));
+    a.complete_depth = 0;
+    if (!prepare_kernels(f, e)) {
+        cudaFree(block);
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    *out = holder.release();
+    return 0;
+}
+
+void mlk_cuda_forest_release(mlk_dev_forest* forest) {
+    if (!forest) return;
+    {
+        mlk::cuda::DeviceGuard guard(forest->f.device);
+        for (int i = 0; i < forest->f.nblocks; ++i) cudaFree(forest->f.blocks[i]);
+    }
+    delete forest;
+}
+
+static int device_call(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
+                       int32_t* leaves, void* stream, char* err, size_t errlen) {
+    using namespace mlk::cuda;
+    if (batch == 0) return 0;
+    std::string e;
+    DeviceGuard guard(forest->f.device);
+    const size_t scratch = scratch_bytes(forest->f);
+    void* tmp = nullptr;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (scratch && !ok(cudaMallocAsync(&tmp, scratch, st), "cudaMallocAsync", e)) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    bool good = true;
+    if (injected("launch")) {
+        e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
+        good = false;
+    } else {
+        good = launch_forest(forest->f, dtype, x, static_cast<long long>(batch), out, leaves, st, e,
+                             static_cast<int*>(tmp));
+    }
+    if (tmp) cudaFreeAsync(tmp, st);
+    if (!good) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    return 0;
+}
+
+int mlk_cuda_predict_device(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
+                            void* stream, char* err, size_t errlen) {
+    return device_call(forest, dtype, x, batch, out, nullptr, stream, err, errlen);
+}
+
+int mlk_cuda_leaves_device(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,
+                           void* stream, char* err, size_t errlen) {
+    return device_call(forest, dtype, x, batch, nullptr, leaves, stream, err, errlen);
+}
+
+int mlk_cuda_predict_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
+                          char* err, size_t errlen) {
+    if (batch == 0) return 0;
+    return mlk::cuda::run_host<double>(forest->f, dtype, x, batch, out, static_cast<size_t>(forest->f.args.K), false,
+                                       err, errlen);
+}
+
+int mlk_cuda_leaves_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,
+                         char* err, size_t errlen) {
+    if (batch == 0) return 0;
+    return mlk::cuda::run_host<int32_t>(forest->f, dtype, x, batch, leaves, static_cast<size_t>(forest->f.args.T),
+                                        true, err, errlen);
+}
+
+}  // extern "C"

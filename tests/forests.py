@@ -1,0 +1,63 @@
+"""Test models: random ensembles over every missing-value mode, and inputs
+full of the values that sit exactly on split rules (NaN, signed zeros,
+LightGBM's zero band, infinities, thresholds themselves)."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from montlok import export
+
+GRID = np.array([-1.5, -0.25, 0.0, 0.5, 2.0])
+SPECIALS = [np.nan, 0.0, -0.0, 1e-35, -1e-36, 1e-36, np.inf, -np.inf, 1e-300, -1e-300, *GRID]
+
+
+def random_model(rng: np.random.Generator, features: int = 5, decision: str = "le", cast: str = "f64",
+                 trees: int = 40, outputs: int = 1, link: str = "identity", aggregate: str = "sum",
+                 max_depth: int = 8, inf_thresholds: float = 0.0, base=0.25, sigmoid_scale: float = 1.0,
+                 preprocess=None, share: bool = False) -> bytes:
+    """Trees of random depth; every split a random feature, threshold (grid or
+    normal, optionally infinite), default side and missing mode."""
+    nodes = export.Nodes()
+    roots = []
+    for _ in range(trees):
+        depth = int(rng.integers(1, max_depth + 1))
+
+        def grow(level: int) -> int:
+            if level == depth or (level > 0 and rng.random() < 0.2):
+                return nodes.add(value=float(rng.normal()))
+            flags = int(rng.integers(2)) | (int(rng.integers(3)) << 1)
+            if rng.random() < inf_thresholds:
+                threshold = float(rng.choice([np.inf, -np.inf]))
+            elif rng.random() < 0.5:
+                threshold = float(rng.choice(GRID))
+            else:
+                threshold = float(rng.normal())
+            i = nodes.add(feature=int(rng.integers(features)), threshold=threshold, flags=flags)
+            nodes.left[i] = grow(level + 1)
+            nodes.right[i] = grow(level + 1)
+            return i
+
+        roots.append(grow(0))
+    if share and len(roots) > 1:
+        roots[-1] = roots[0]
+    tree_outputs = [t % outputs for t in range(trees)]
+    return export.tree_ensemble(nodes, roots, tree_outputs, features=features, outputs=outputs, decision=decision,
+                                feature_cast=cast, aggregate=aggregate, link=link, base_score=base,
+                                sigmoid_scale=sigmoid_scale, preprocess=preprocess).to_bytes()
+
+
+def edge_inputs(rng: np.random.Generator, rows: int, features: int, special: float = 0.4) -> np.ndarray:
+    x = rng.normal(size=(rows, features))
+    pick = rng.random((rows, features)) < special
+    x[pick] = rng.choice(np.array(SPECIALS), size=int(pick.sum()))
+    return x
+
+
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    """Equal as float64 bit patterns, every NaN counting as equal to any NaN."""
+    a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
+    if a.shape != b.shape:
+        return False
+    nan = np.isnan(a)
+    return bool(np.array_equal(nan, np.isnan(b)) and np.array_equal(a[~nan].view(np.int64), b[~nan].view(np.int64)))

@@ -1,0 +1,183 @@
+"""Parity of the CUDA path with the CPU oracle, through the C ABI.
+
+Every case compares, bit for bit, the predictions and the leaf index of every
+(row, tree) that libmontlok.so computes on the GPU with the oracle's (the
+plain-C restatement of the reference, itself pinned to the reference in
+test_oracle.py): the five benchmark recipes at test sizes, random ensembles
+over every missing-value mode with inputs on the split rules, every link,
+mean aggregation, float32 inputs, preprocess, multi-pass outputs, the
+global-memory key path, shared nodes and infinite thresholds.
+"""
+
+from __future__ import annotations
+
+import os
+import threading
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+import montlok
+from forests import edge_inputs, random_model, same_bits
+from montlok import export, synth
+from oracle import Oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def check(model: bytes, x: np.ndarray, leaves: bool = True) -> None:
+    m = montlok.load(model)
+    o = Oracle(model)
+    got = m.predict(x)
+    want = o.predict(x)
+    assert same_bits(got.reshape(want.shape), want), "predictions differ from the oracle"
+    if leaves:
+        np.testing.assert_array_equal(m.predict_leaves(x).reshape(len(want), -1), o.leaves(x))
+
+
+RECIPES = {
+    "c1": (lambda: synth.model_c1().to_bytes(), lambda: synth.inputs_c1(batch=2000)),
+    "c2": (lambda: synth.model_c2(trees=120).to_bytes(), lambda: synth.inputs_c2(batch=3000)),
+    "c3": (lambda: synth.model_c3(trees=6, samples=20_000).to_bytes(), lambda: synth.inputs_c3(batch=1500)),
+    "c4": (lambda: synth.model_c4(rounds=14).to_bytes(), lambda: synth.inputs_c4(batch=1500)),
+    "c5": (lambda: synth.model_c5(trees=150).to_bytes(), lambda: synth.inputs_c5(batch=64)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(RECIPES))
+def test_benchmark_recipes(gpu, name):
+    make_model, make_x = RECIPES[name]
+    check(make_model(), make_x())
+
+
+@pytest.mark.parametrize("decision", ["le", "lt"])
+@pytest.mark.parametrize("cast", ["f64", "f32"])
+@pytest.mark.parametrize("inf", [0.0, 0.15])
+def test_edge_values_every_missing_mode(gpu, decision, cast, inf):
+    rng = np.random.default_rng([len(decision), len(cast), int(inf * 100)])
+    model = random_model(rng, features=7, decision=decision, cast=cast, trees=150, inf_thresholds=inf)
+    check(model, edge_inputs(rng, 700, 7))
+
+
+@pytest.mark.parametrize("link, outputs, aggregate", [
+    ("sigmoid", 1, "sum"), ("exp", 1, "sum"), ("softmax", 3, "sum"), ("softmax", 12, "sum"),
+    ("identity", 5, "mean"), ("exp", 4, "mean"), ("identity", 11, "sum"), ("sigmoid", 9, "mean"),
+])
+def test_links_outputs_and_aggregates(gpu, link, outputs, aggregate):
+    rng = np.random.default_rng(outputs * 7 + len(link))
+    model = random_model(rng, features=6, trees=200, outputs=outputs, link=link, aggregate=aggregate,
+                         base=list(rng.normal(size=outputs)), sigmoid_scale=0.7)
+    check(model, edge_inputs(rng, 400, 6, special=0.2))
+
+
+@pytest.mark.parametrize("cast", ["f64", "f32"])
+def test_preprocess_then_cast(gpu, cast):
+    rng = np.random.default_rng(5)
+    pre = {"mean": rng.normal(size=6) * 3, "scale": rng.uniform(0.5, 2.0, 6), "clip": (-1.2, 1.7)}
+    model = random_model(rng, features=6, cast=cast, trees=90, preprocess=pre)
+    x = edge_inputs(rng, 500, 6) * 2 + pre["mean"]
+    check(model, x)
+
+
+def test_float32_inputs(gpu):
+    rng = np.random.default_rng(11)
+    for cast in ("f64", "f32"):
+        model = random_model(rng, features=9, cast=cast, trees=80)
+        check(model, edge_inputs(rng, 600, 9).astype(np.float32))
+
+
+@pytest.mark.parametrize("rows", [1, 2, 31, 32, 33, 63, 65, 4099])
+def test_ragged_batches(gpu, rows):
+    rng = np.random.default_rng(rows)
+    model = random_model(rng, features=4, trees=70)
+    check(model, edge_inputs(rng, rows, 4))
+
+
+def test_single_row_and_empty_batch(gpu):
+    rng = np.random.default_rng(2)
+    model = random_model(rng, features=5, trees=30)
+    m = montlok.load(model)
+    x = edge_inputs(rng, 10, 5)
+    block = m.predict(x)
+    rows = np.stack([m.predict(r) for r in x])
+    assert same_bits(block, rows)
+    assert m.predict(np.zeros((0, 5))).shape == (0, 1)
+
+
+def test_shared_nodes_and_infinite_thresholds(gpu):
+    """Mirrors the reference test of the same name (tests/python/test_trees.py:275-283)."""
+    nodes = export.Nodes()
+    split = nodes.add(feature=0, threshold=-np.inf, flags=1 | (1 << 1))
+    nodes.left[split] = nodes.add(value=1.0)
+    nodes.right[split] = nodes.add(value=2.0)
+    model = export.tree_ensemble(nodes, [split, split], [0, 0], features=1).to_bytes()
+    x = np.array([[-np.inf], [-1e308], [0.0], [np.inf], [np.nan]])
+    np.testing.assert_array_equal(montlok.load(model).predict(x)[:, 0], [2.0, 4.0, 4.0, 4.0, 2.0])
+    check(model, x)
+
+
+def test_many_features_use_global_key_tables(gpu):
+    """Over ~1750 (feature, rule) slots the key tables move to global memory."""
+    rng = np.random.default_rng(3)
+    model = random_model(rng, features=1200, trees=400, max_depth=10)
+    check(model, edge_inputs(rng, 300, 1200, special=0.3))
+
+
+def test_device_buffers_match_host_buffers(gpu):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(4)
+    model = random_model(rng, features=8, trees=100, outputs=3, link="softmax")
+    m = montlok.load(model)
+    x = edge_inputs(rng, 1000, 8)
+    host = m.predict(x)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((1000, 3), dtype=torch.float64, device="cuda")
+    m.predict(xd, out=out)
+    torch.cuda.synchronize()
+    assert same_bits(out.cpu().numpy(), host)
+
+
+def test_concurrent_callers_get_the_same_bits(gpu):
+    rng = np.random.default_rng(6)
+    model = random_model(rng, features=6, trees=120, cast="f32", decision="lt")
+    m = montlok.load(model)
+    rows = edge_inputs(rng, 64, 6)
+    expected = m.predict(rows)
+    with ThreadPoolExecutor(6) as pool:
+        got = list(pool.map(lambda r: m.predict(r), rows))
+    assert same_bits(np.stack(got), expected)
+
+
+def test_stream_is_stateless_predict(gpu):
+    rng = np.random.default_rng(8)
+    m = montlok.load(random_model(rng, features=4, trees=20))
+    live = m.stream()
+    x = edge_inputs(rng, 20, 4)
+    for row in x:
+        assert same_bits(live.step(row), m.predict(row))
+
+
+@pytest.mark.parametrize("fault", ["alloc", "copy", "launch"])
+def test_injected_cuda_failures_are_clean_errors(gpu, fault):
+    rng = np.random.default_rng(9)
+    m = montlok.load(random_model(rng, features=4, trees=10))
+    x = edge_inputs(rng, 50, 4)
+    expected = m.predict(x)
+    errors = []
+
+    def call():  # a fresh thread has no workspace yet, so "alloc" bites
+        try:
+            m.predict(x)
+        except RuntimeError as e:
+            errors.append(str(e))
+
+    os.environ["MONTLOK_FAULT_INJECT"] = fault
+    try:
+        t = threading.Thread(target=call)
+        t.start()
+        t.join()
+    finally:
+        del os.environ["MONTLOK_FAULT_INJECT"]
+    assert errors and "injected fault" in errors[0]
+    assert same_bits(m.predict(x), expected)
