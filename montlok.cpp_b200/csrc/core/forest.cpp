@@ -80,6 +80,60 @@ int variant_of(uint8_t flags, double t, bool le) noexcept {
     return default_left ? kZeroLeft : kZeroRight;
 }
 
+// The complete-tree view of a single-output forest no deeper than 8 levels
+// (see ForestImage). A leaf above the last level becomes splits that always
+// go left (T = INT32_MAX, never exceeded) down to copies of itself.
+void build_heap_view(ForestImage& img) {
+    constexpr int kMaxDepth = 8;
+    if (img.outputs != 1) return;
+    int D = 1;
+    for (const int32_t d : img.depth) D = std::max(D, static_cast<int>(d));
+    if (D > kMaxDepth) return;
+    const size_t splits = (size_t{1} << D) - 1, leaves = size_t{1} << D, T = static_cast<size_t>(img.trees);
+    img.heap_words.assign(T * splits * 2, 0);
+    img.heap_node_id.assign(T * splits, -1);
+    img.heap_leaf.assign(T * leaves, 0.0);
+    img.heap_leaf_id.assign(T * leaves, -1);
+    bool f32 = true;
+    struct Item {
+        size_t heap;
+        int level;
+        int32_t node;
+    };
+    std::vector<Item> stack;
+    for (size_t t = 0; t < T; ++t) {
+        stack.assign(1, Item{0, 0, img.roots[t]});
+        while (!stack.empty()) {
+            const Item it = stack.back();
+            stack.pop_back();
+            const bool split = img.feature[static_cast<size_t>(it.node)] >= 0;
+            if (it.level == D) {  // a real leaf: depth D bounds every path
+                const double v = img.leaf_value[static_cast<size_t>(it.node)];
+                img.heap_leaf[t * leaves + (it.heap - splits)] = v;
+                img.heap_leaf_id[t * leaves + (it.heap - splits)] = it.node;
+                f32 = f32 && static_cast<double>(static_cast<float>(v)) == v;
+                continue;
+            }
+            int32_t* w = &img.heap_words[(t * splits + it.heap) * 2];
+            if (split) {
+                const int32_t* nw = &img.node_words[static_cast<size_t>(it.node) * 4];
+                w[0] = nw[0];
+                w[1] = nw[1];
+                img.heap_node_id[t * splits + it.heap] = it.node;
+                stack.push_back(Item{2 * it.heap + 2, it.level + 1, nw[3]});
+                stack.push_back(Item{2 * it.heap + 1, it.level + 1, nw[2]});
+            } else {
+                w[0] = kNeverRight;
+                w[1] = img.pad_slot;
+                stack.push_back(Item{2 * it.heap + 2, it.level + 1, it.node});
+                stack.push_back(Item{2 * it.heap + 1, it.level + 1, it.node});
+            }
+        }
+    }
+    img.complete_depth = D;
+    img.heap_leaf_f32 = f32;
+}
+
 }  // namespace
 
 std::unique_ptr<ForestImage> build_forest(const Archive& a, const json::Value& spec, const json::Value& config,
@@ -218,6 +272,7 @@ std::unique_ptr<ForestImage> build_forest(const Archive& a, const json::Value& s
     img->threshold = std::move(threshold);
     img->feature = std::move(feature);
     img->flags = std::move(flags);
+    build_heap_view(*img);
     return img;
 }
 

@@ -95,7 +95,9 @@ public:
         v_.clip_lo = pre.lo;
         v_.clip_hi = pre.hi;
         v_.complete_depth = img.complete_depth;
+        v_.heap_leaf_f32 = img.heap_leaf_f32;
         v_.heap_words = img.heap_words.empty() ? nullptr : img.heap_words.data();
+        v_.heap_node_id = img.heap_node_id.empty() ? nullptr : img.heap_node_id.data();
         v_.heap_leaf = img.heap_leaf.empty() ? nullptr : img.heap_leaf.data();
         v_.heap_leaf_id = img.heap_leaf_id.empty() ? nullptr : img.heap_leaf_id.data();
     }

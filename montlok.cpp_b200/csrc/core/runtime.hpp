@@ -124,13 +124,16 @@ struct ForestImage {
     std::vector<int32_t> feature;     // [nodes], -1 for leaves
     std::vector<uint8_t> flags;       // [nodes]
 
-    // Complete-tree view: every tree a complete binary tree of `complete_depth`
-    // levels in heap order. Empty when the model is not of that shape.
+    // Complete-tree view: every tree as a complete binary tree of
+    // `complete_depth` levels in heap order (children of i at 2i+1, 2i+2),
+    // shallower leaves padded with splits that always go left. Built for
+    // single-output models of depth <= 8; complete_depth is 0 otherwise.
     int32_t complete_depth = 0;
-    std::vector<int32_t> heap_words;  // [trees * (2^d - 1) * 2]: T, slot
-    std::vector<double> heap_leaf;    // [trees * 2^d]
-    std::vector<int32_t> heap_leaf_id;// [trees * 2^d]: node index of each leaf
-    bool heap_leaf_f32 = false;       // every leaf value is exactly a float
+    std::vector<int32_t> heap_words;    // [trees * (2^d - 1) * 2]: T, slot
+    std::vector<int32_t> heap_node_id;  // [trees * (2^d - 1)]: file node, -1 for padding
+    std::vector<double> heap_leaf;      // [trees * 2^d]
+    std::vector<int32_t> heap_leaf_id;  // [trees * 2^d]: file node of each leaf
+    bool heap_leaf_f32 = false;         // every leaf value is exactly a float
 };
 
 // Builds the image from a validated spec/archive; throws Error like the

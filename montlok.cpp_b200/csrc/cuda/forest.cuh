@@ -27,17 +27,23 @@ struct ForestArgs {
     const int* counts;          // [K]
     const double* threshold;    // [nodes]
     const int* feature;         // [nodes]
-    // Complete-tree view (complete_depth > 0).
-    int complete_depth;
-    const int2* heap_words;     // [T * (2^d - 1)]: T, slot
-    const double* heap_leaf;    // [T * 2^d]
-    const int* heap_leaf_id;    // [T * 2^d]
+    int* status;                // mapped host word: nonzero after a kernel gave up waiting
+};
+
+// Complete-tree layout (heap_kernels.cu); depth 0 when the model has none.
+struct HeapArgs {
+    int depth, rows, leaf32;
+    const unsigned char* trees;  // [T] records of heap_record_bytes(depth, leaf32)
+    const int* node_ids;         // [T * (2^depth - 1)]: file node of each heap split, -1 for padding
+    int* status;
 };
 
 struct DevForest {
     int device = 0;
     int sm_count = 0;
     ForestArgs args{};
+    HeapArgs heap{};
+    int* status_host = nullptr;  // the status word as the host sees it
     void* blocks[20] = {};  // device allocations, freed with the forest
     int nblocks = 0;
 };
@@ -55,5 +61,12 @@ size_t scratch_bytes(const DevForest& f);
 
 // One-time per-device kernel attributes (dynamic shared memory limits).
 bool prepare_kernels(const DevForest& f, std::string& err);
+
+// Complete-tree kernels: rows per CTA that fit shared memory (0: none),
+// bytes of one tree record, and the launch.
+int heap_plan_rows(int slots, int depth, bool leaf32);
+int heap_record_bytes(int depth, bool leaf32);
+bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
+                 std::string& err);
 
 }  // namespace mlk::cuda

@@ -29,96 +29,11 @@
 #include <mutex>
 #include <vector>
 
+#include "device_common.cuh"
 #include "forest.cuh"
 
 namespace mlk::cuda {
 namespace {
-
-constexpr int kTreeBlock = 64;  // trees per partial sum
-constexpr int kMaxOut = 8;      // outputs held in registers per pass
-constexpr int kIlp = 4;         // trees one lane walks side by side
-constexpr int kStage = 33;      // padded row length of the transpose tile
-constexpr int kStageBytes = 32 * kStage * 8;
-constexpr double kZeroThr = static_cast<double>(1e-35f);  // LightGBM kZeroThreshold
-
-__host__ __device__ constexpr int align16(int n) { return (n + 15) & ~15; }
-__host__ __device__ constexpr int key_bytes(int slots) { return align16(slots * 32 * 4); }
-
-__device__ __forceinline__ int key32(float v) {
-    const unsigned b = __float_as_uint(v);
-    const int m = static_cast<int>(b & 0x7fffffffu);
-    return (b >> 31) ? -m : m;
-}
-
-__device__ __forceinline__ double load_x(const float* p) { return static_cast<double>(__ldg(p)); }
-__device__ __forceinline__ double load_x(const double* p) { return __ldg(p); }
-
-// Preprocess and cast of one raw value (reference runtime.cpp:532-552 and the
-// cast of trees.cpp:275); std::max/std::min written out so NaN stays NaN.
-__device__ __forceinline__ double finish(const ForestArgs& a, double v, double mean, double scale) {
-    if (a.standardize) v = __ddiv_rn(__dsub_rn(v, mean), scale);
-    if (a.clip) {
-        v = (v < a.lo) ? a.lo : v;
-        v = (a.hi < v) ? a.hi : v;
-    }
-    if (a.cast_f32) v = static_cast<double>(__double2float_rn(v));
-    return v;
-}
-
-__device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, double v) {
-    const bool nan = v != v;
-    const int k = a.cast_f32 ? key32(__double2float_rn(v)) : key32(__double2float_rd(v));
-    const bool zero = nan || fabs(v) <= kZeroThr;
-    if (s.x >= 0) col[s.x * 32] = nan ? INT_MAX : k;
-    if (s.y >= 0) col[s.y * 32] = nan ? INT_MIN : k;
-    if (s.z >= 0) col[s.z * 32] = zero ? INT_MAX : k;
-    if (s.w >= 0) col[s.w * 32] = zero ? INT_MIN : k;
-}
-
-template <typename XT>
-__device__ void prepare_group(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch,
-                              int* keys, double* stage, int lane) {
-    for (int f0 = 0; f0 < a.F; f0 += 32) {
-        const int feat = f0 + lane;
-        const bool live = feat < a.F;
-        double mean = 0.0, scale = 1.0;
-        if (live && a.standardize) {
-            mean = __ldg(a.pre_mean + feat);
-            scale = __ldg(a.pre_scale + feat);
-        }
-#pragma unroll 8
-        for (int i = 0; i < 32; ++i) {
-            const long long row = row0 + i;
-            double v = 0.0;
-            if (live && row < batch) v = finish(a, load_x(x + row * a.F + feat), mean, scale);
-            stage[i * kStage + lane] = v;
-        }
-        __syncwarp();
-        const int nf = min(32, a.F - f0);
-        for (int j = 0; j < nf; ++j) put_keys(a, keys + lane, __ldg(a.slot_of + f0 + j), stage[lane * kStage + j]);
-        __syncwarp();
-    }
-    keys[a.pad_slot * 32 + lane] = INT_MIN;
-    __syncwarp();
-}
-
-// The split decided on doubles, for a float64 model whose keys tied.
-template <typename XT>
-__device__ __noinline__ bool exact_right(const ForestArgs& a, const XT* __restrict__ x, long long row,
-                                         long long batch, int idx) {
-    const int feat = __ldg(a.feature + idx);
-    const double t = __ldg(a.threshold + idx);
-    double v = 0.0;  // padding rows were prepared as 0.0
-    if (row < batch) {
-        double mean = 0.0, scale = 1.0;
-        if (a.standardize) {
-            mean = __ldg(a.pre_mean + feat);
-            scale = __ldg(a.pre_scale + feat);
-        }
-        v = finish(a, load_x(x + row * a.F + feat), mean, scale);
-    }
-    return a.le ? (v > t) : !(v < t);
-}
 
 template <bool TIES, typename XT>
 __device__ __forceinline__ int step(const ForestArgs& a, const int* col, int idx, const XT* x, long long row,
@@ -171,73 +86,6 @@ __device__ __forceinline__ void walk_block(const ForestArgs& a, const int* col, 
     }
 }
 
-// ---------------------------------------------------------------------------
-// Link functions: the reference's exp (kernels.hpp:220-253) — clamp to
-// [-708, 708], n = round(x / ln 2) through the 1.5 * 2^52 shifter, Cody-Waite
-// reduction r = (x - n ln2_hi) - n ln2_lo, exp(r) - 1 by the degree-13 Taylor
-// series in Horner form, and 2^n assembled in the exponent bits.
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ double vexp(double x) {
-    constexpr double kInvLn2 = 1.4426950408889634074;
-    constexpr double kLn2Hi = 6.93147180369123816490e-01;
-    constexpr double kLn2Lo = 1.90821492927058770002e-10;
-    constexpr double kShifter = 6755399441055744.0;
-    constexpr double c[13] = {
-        1.0 / 6227020800.0, 1.0 / 479001600.0, 1.0 / 39916800.0, 1.0 / 3628800.0, 1.0 / 362880.0,
-        1.0 / 40320.0,      1.0 / 5040.0,      1.0 / 720.0,      1.0 / 120.0,     1.0 / 24.0,
-        1.0 / 6.0,          0.5,               1.0,
-    };
-    x = (x < -708.0) ? -708.0 : x;
-    x = (x > 708.0) ? 708.0 : x;
-    const double shifted = __dadd_rn(__dmul_rn(x, kInvLn2), kShifter);
-    const double n = __dsub_rn(shifted, kShifter);
-    const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(n, kLn2Hi)), __dmul_rn(n, kLn2Lo));
-    double p = c[0];
-#pragma unroll
-    for (int i = 1; i < 13; ++i) p = __dadd_rn(__dmul_rn(p, r), c[i]);
-    p = __dadd_rn(__dmul_rn(p, r), 1.0);
-    const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(shifted)) -
-                                    static_cast<unsigned long long>(__double_as_longlong(kShifter));
-    return __dmul_rn(p, __longlong_as_double(static_cast<long long>((bits + 1023ull) << 52)));
-}
-
-template <int KC>
-__device__ __forceinline__ void apply_link(const ForestArgs& a, double (&v)[KC], int kc) {
-    if (a.link == 1) {
-#pragma unroll
-        for (int j = 0; j < KC; ++j) {
-            if (j < kc) {
-                const double s = __dmul_rn(v[j], a.sigmoid_scale);
-                v[j] = __ddiv_rn(1.0, __dadd_rn(1.0, vexp(__dsub_rn(0.0, s))));
-            }
-        }
-    } else if (a.link == 3) {
-#pragma unroll
-        for (int j = 0; j < KC; ++j) {
-            if (j < kc) v[j] = vexp(v[j]);
-        }
-    } else if (a.link == 2) {
-        double peak = v[0];
-#pragma unroll
-        for (int j = 1; j < KC; ++j) {
-            if (j < kc) peak = (peak < v[j]) ? v[j] : peak;
-        }
-        double total = 0.0;
-#pragma unroll
-        for (int j = 0; j < KC; ++j) {
-            if (j < kc) {
-                v[j] = vexp(__dsub_rn(v[j], peak));
-                total = __dadd_rn(total, v[j]);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < KC; ++j) {
-            if (j < kc) v[j] = __ddiv_rn(v[j], total);
-        }
-    }
-}
-
 template <bool TIES, bool LEAVES, int KC, bool GLOBAL_KEYS, typename XT>
 __global__ void __launch_bounds__(64) forest_kernel(const ForestArgs a, const XT* __restrict__ x, long long batch,
                                                      double* __restrict__ out, int* __restrict__ leaves, int k0,
@@ -254,7 +102,7 @@ __global__ void __launch_bounds__(64) forest_kernel(const ForestArgs a, const XT
     const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
     for (long long g = me; g < groups; g += all_warps) {
         const long long row0 = g * 32;
-        prepare_group(a, x, row0, batch, keys, stage, lane);
+        prepare_group<32>(a, x, row0, batch, keys, stage, lane);
         const long long row = row0 + lane;
         const int* col = keys + lane;
         double acc[KC];
@@ -393,6 +241,7 @@ size_t scratch_bytes(const DevForest& f) {
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
                    cudaStream_t stream, std::string& err, int* scratch) {
     if (batch <= 0) return true;
+    if (out && !leaves && f.heap.depth > 0) return launch_heap(f, dtype, x, batch, out, stream, err);
     const ForestArgs& a = f.args;
     const Shape s = shape_of(a);
     const bool ties = !a.cast_f32;

@@ -37,8 +37,9 @@ typedef struct mlk_forest_view {
     const double* pre_scale;     /* [features] or NULL */
     double clip_lo, clip_hi;
     /* Complete-tree view (complete_depth > 0): heap-ordered splits and leaves. */
-    int32_t complete_depth;
+    int32_t complete_depth, heap_leaf_f32;
     const int32_t* heap_words;   /* [trees * (2^d - 1) * 2]: T, slot */
+    const int32_t* heap_node_id; /* [trees * (2^d - 1)] */
     const double* heap_leaf;     /* [trees * 2^d] */
     const int32_t* heap_leaf_id; /* [trees * 2^d] */
 } mlk_forest_view;

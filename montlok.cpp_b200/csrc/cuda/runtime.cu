@@ -274,6 +274,10 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
         if (good) good = ok(cudaStreamSynchronize(w->stream[s]), "cudaStreamSynchronize", e);
         else cudaStreamSynchronize(w->stream[s]);
     }
+    if (good && f.status_host && *reinterpret_cast<volatile int*>(f.status_host) != 0) {
+        e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
+        good = false;
+    }
     if (!good) {
         put_error(err, errlen, e);
         return kInternal;
@@ -413,9 +417,64 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     a.counts = reinterpret_cast<const int*>(at(i_counts));
     a.threshold = reinterpret_cast<const double*>(at(i_thr));
     a.feature = reinterpret_cast<const int*>(at(i_feat));
-    a.complete_depth = 0;
-    if (!prepare_kernels(f, e)) {
+    // The status word kernels raise when a bounded wait runs out: mapped
+    // pinned memory, so the host reads it without a copy.
+    void* status = nullptr;
+    if (!ok(cudaHostAlloc(&status, sizeof(int), cudaHostAllocMapped), "cudaHostAlloc", e) ||
+        !ok(cudaHostGetDevicePointer(reinterpret_cast<void**>(&a.status), status, 0), "cudaHostGetDevicePointer", e)) {
+        if (status) cudaFreeHost(status);
         cudaFree(block);
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    f.status_host = static_cast<int*>(status);
+    *f.status_host = 0;
+    f.heap.status = a.status;
+    // Complete-tree records: [2^d - 1 splits (T, slot)] [2^d leaves], 16-byte aligned.
+    const int D = v->complete_depth;
+    const int rows = D > 0 ? heap_plan_rows(v->slots, D, v->heap_leaf_f32 != 0) : 0;
+    if (rows > 0) {
+        const bool f32 = v->heap_leaf_f32 != 0;
+        const size_t splits = (size_t{1} << D) - 1, leaves = size_t{1} << D;
+        const size_t rec = static_cast<size_t>(heap_record_bytes(D, f32));
+        std::vector<unsigned char> host(T * rec, 0);
+        for (size_t t = 0; t < T; ++t) {
+            unsigned char* r = host.data() + t * rec;
+            std::memcpy(r, v->heap_words + t * splits * 2, splits * 8);
+            for (size_t j = 0; j < leaves; ++j) {
+                const double value = v->heap_leaf[t * leaves + j];
+                if (f32) {
+                    const float fv = static_cast<float>(value);
+                    std::memcpy(r + splits * 8 + j * 4, &fv, 4);
+                } else {
+                    std::memcpy(r + splits * 8 + j * 8, &value, 8);
+                }
+            }
+        }
+        void* trees = nullptr;
+        void* ids = nullptr;
+        if (!device_alloc(&trees, host.size(), e) ||
+            !ok(cudaMemcpy(trees, host.data(), host.size(), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+            !device_alloc(&ids, T * splits * 4, e) ||
+            !ok(cudaMemcpy(ids, v->heap_node_id, T * splits * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
+            if (trees) cudaFree(trees);
+            if (ids) cudaFree(ids);
+            cudaFreeHost(status);
+            cudaFree(block);
+            put_error(err, errlen, e);
+            return kInternal;
+        }
+        f.blocks[f.nblocks++] = trees;
+        f.blocks[f.nblocks++] = ids;
+        f.heap.depth = D;
+        f.heap.rows = rows;
+        f.heap.leaf32 = f32;
+        f.heap.trees = static_cast<const unsigned char*>(trees);
+        f.heap.node_ids = static_cast<const int*>(ids);
+    }
+    if (!prepare_kernels(f, e)) {
+        cudaFreeHost(status);
+        for (int i = 0; i < f.nblocks; ++i) cudaFree(f.blocks[i]);
         put_error(err, errlen, e);
         return kInternal;
     }
@@ -428,6 +487,7 @@ void mlk_cuda_forest_release(mlk_dev_forest* forest) {
     {
         mlk::cuda::DeviceGuard guard(forest->f.device);
         for (int i = 0; i < forest->f.nblocks; ++i) cudaFree(forest->f.blocks[i]);
+        if (forest->f.status_host) cudaFreeHost(forest->f.status_host);
     }
     delete forest;
 }
