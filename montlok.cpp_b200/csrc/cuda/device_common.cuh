@@ -51,30 +51,47 @@ __device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, 
     if (s.w >= 0) col[s.w * STRIDE] = zero ? INT_MIN : k;
 }
 
-template <int STRIDE, typename XT>
+// Builds the key table columns of 32 rows starting at row0: the warp reads
+// TILE features of all 32 rows at a time, coalesced (TILE consecutive values
+// per row), stages them in a padded [32][TILE + 1] tile, and then each lane
+// (one row) turns its TILE values into keys. `keys` points at the warp's first
+// column; slot s of the lane's row is keys[s * STRIDE + lane].
+template <int STRIDE, int TILE, typename XT>
 __device__ void prepare_group(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch,
-                              int* keys, double* stage, int lane) {
-    for (int f0 = 0; f0 < a.F; f0 += 32) {
-        const int feat = f0 + lane;
-        const bool live = feat < a.F;
+                              int* keys, double* stage, int lane, int f_begin = 0, int f_end = -1,
+                              bool pad = true) {
+    static_assert(TILE == 16 || TILE == 32, "tiles of 16 or 32 features");
+    constexpr int kPerLoad = 32 / TILE;  // rows covered by one warp-wide load
+    const int sub = lane / TILE, f_in = lane % TILE;
+    if (f_end < 0) f_end = a.F;
+    for (int f0 = f_begin; f0 < f_end; f0 += TILE) {
+        const int feat = f0 + f_in;
+        const bool live = feat < f_end;
         double mean = 0.0, scale = 1.0;
         if (live && a.standardize) {
             mean = __ldg(a.pre_mean + feat);
             scale = __ldg(a.pre_scale + feat);
         }
-#pragma unroll 8
-        for (int i = 0; i < 32; ++i) {
-            const long long row = row0 + i;
-            double v = 0.0;
-            if (live && row < batch) v = finish(a, load_x(x + row * a.F + feat), mean, scale);
-            stage[i * kStage + lane] = v;
+        // All loads of the tile first, so their latencies overlap.
+        double raw[32 / kPerLoad];
+#pragma unroll
+        for (int i = 0; i < 32 / kPerLoad; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            raw[i] = (live && row < batch) ? load_x(x + row * a.F + feat) : 0.0;
+        }
+#pragma unroll
+        for (int i = 0; i < 32 / kPerLoad; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            stage[(i * kPerLoad + sub) * (TILE + 1) + f_in] = (live && row < batch) ? finish(a, raw[i], mean, scale) : 0.0;
         }
         __syncwarp();
-        const int nf = min(32, a.F - f0);
-        for (int j = 0; j < nf; ++j) put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), stage[lane * kStage + j]);
+        const int nf = min(TILE, f_end - f0);
+        for (int j = 0; j < nf; ++j) {
+            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), stage[lane * (TILE + 1) + j]);
+        }
         __syncwarp();
     }
-    keys[a.pad_slot * STRIDE + lane] = INT_MIN;
+    if (pad) keys[a.pad_slot * STRIDE + lane] = INT_MIN;
     __syncwarp();
 }
 

@@ -32,8 +32,8 @@ struct ForestArgs {
 
 // Complete-tree layout (heap_kernels.cu); depth 0 when the model has none.
 struct HeapArgs {
-    int depth, rows, leaf32;
-    const unsigned char* trees;  // [T] records of heap_record_bytes(depth, leaf32)
+    int depth, rows, leaf32, buffers;
+    const unsigned char* trees;  // whole chunks of heap_record_bytes(depth, leaf32) records, inert trees last
     const int* node_ids;         // [T * (2^depth - 1)]: file node of each heap split, -1 for padding
     int* status;
 };
@@ -62,10 +62,11 @@ size_t scratch_bytes(const DevForest& f);
 // One-time per-device kernel attributes (dynamic shared memory limits).
 bool prepare_kernels(const DevForest& f, std::string& err);
 
-// Complete-tree kernels: rows per CTA that fit shared memory (0: none),
-// bytes of one tree record, and the launch.
-int heap_plan_rows(int slots, int depth, bool leaf32);
+// Complete-tree kernels: rows per CTA and chunk buffers that fit shared
+// memory (false: none), bytes of one tree record, trees per chunk, launch.
+bool heap_plan(int slots, int depth, bool leaf32, int& rows, int& buffers);
 int heap_record_bytes(int depth, bool leaf32);
+int heap_chunk_trees();
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
 

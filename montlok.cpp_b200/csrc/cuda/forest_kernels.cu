@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(64) forest_kernel(const ForestArgs a, const XT
     const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
     for (long long g = me; g < groups; g += all_warps) {
         const long long row0 = g * 32;
-        prepare_group<32>(a, x, row0, batch, keys, stage, lane);
+        prepare_group<32, 32>(a, x, row0, batch, keys, stage, lane);
         const long long row = row0 + lane;
         const int* col = keys + lane;
         double acc[KC];

@@ -432,15 +432,28 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     f.heap.status = a.status;
     // Complete-tree records: [2^d - 1 splits (T, slot)] [2^d leaves], 16-byte aligned.
     const int D = v->complete_depth;
-    const int rows = D > 0 ? heap_plan_rows(v->slots, D, v->heap_leaf_f32 != 0) : 0;
-    if (rows > 0) {
+    int rows = 0, buffers = 0;
+    if (D > 0 && heap_plan(v->slots, D, v->heap_leaf_f32 != 0, rows, buffers)) {
         const bool f32 = v->heap_leaf_f32 != 0;
         const size_t splits = (size_t{1} << D) - 1, leaves = size_t{1} << D;
         const size_t rec = static_cast<size_t>(heap_record_bytes(D, f32));
-        std::vector<unsigned char> host(T * rec, 0);
+        // Whole chunks: the tail is inert trees (every split goes left, to
+        // leaves of 0.0), which the kernel walks but never adds.
+        const size_t chunk = static_cast<size_t>(heap_chunk_trees());
+        const size_t padded = (T + chunk - 1) / chunk * chunk;
+        std::vector<unsigned char> host(padded * rec, 0);
+        for (size_t t = 0; t < padded; ++t) {
+            // The kernel reads a split's second word as the byte offset of its
+            // slot in the [slot][rows] key table.
+            int32_t* w = reinterpret_cast<int32_t*>(host.data() + t * rec);
+            const int32_t* src = t < T ? v->heap_words + t * splits * 2 : nullptr;
+            for (size_t i = 0; i < splits; ++i) {
+                w[2 * i] = src ? src[2 * i] : INT32_MAX;
+                w[2 * i + 1] = (src ? src[2 * i + 1] : v->pad_slot) * rows * 4;
+            }
+        }
         for (size_t t = 0; t < T; ++t) {
             unsigned char* r = host.data() + t * rec;
-            std::memcpy(r, v->heap_words + t * splits * 2, splits * 8);
             for (size_t j = 0; j < leaves; ++j) {
                 const double value = v->heap_leaf[t * leaves + j];
                 if (f32) {
@@ -468,6 +481,7 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         f.blocks[f.nblocks++] = ids;
         f.heap.depth = D;
         f.heap.rows = rows;
+        f.heap.buffers = buffers;
         f.heap.leaf32 = f32;
         f.heap.trees = static_cast<const unsigned char*>(trees);
         f.heap.node_ids = static_cast<const int*>(ids);
