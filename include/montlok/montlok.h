@@ -125,6 +125,25 @@ MONTLOK_API int montlok_plugin_load(const char* path);
 MONTLOK_API int montlok_model_predict_device(const montlok_model* model, montlok_dtype dtype, const void* x,
                                              size_t batch, double* out, void* stream);
 
+/* Additive; no counterpart in the reference. montlok_model_predict_device
+ * for callers that cannot allocate GPU memory while they predict: serving
+ * loops whose device memory belongs to another allocator (a framework's
+ * caching pool that has already reserved the GPU) and latency-critical paths
+ * that must not pay for cudaMalloc/cudaFree or the device-wide
+ * synchronisation cudaFree implies. It allocates nothing: the key tables of
+ * each 32-row group live in a static 16 MiB device array of this library
+ * (present on every GPU that loads it, until the process exits), and the
+ * kernel grid is cut to the tables that fit. A model needing more than 16 MiB
+ * for one table (more than 131072 feature/missing-rule slots, about 32768
+ * features) fails with MONTLOK_ERROR_UNSUPPORTED. The model must already be
+ * resident on the current device (after one predict or predict_device call
+ * there), else MONTLOK_ERROR_STATE. The first call on a device looks the
+ * array's device address up, so make it before any stream capture. Calls
+ * share the array: calls whose kernels overlap on the GPU (concurrent
+ * streams) race on it and must be serialised by the caller. */
+MONTLOK_API int montlok_model_predict_device_noalloc(const montlok_model* model, montlok_dtype dtype, const void* x,
+                                                     size_t batch, double* out, void* stream);
+
 /* Additive. The node index (into the file's trees.* tensors) of the leaf each
  * row reaches in each tree: leaves holds batch * trees int32, row-major. The
  * _device form takes device buffers and a stream like predict_device. */

@@ -169,6 +169,14 @@ int montlok_model_predict_device(const montlok_model* model, montlok_dtype dtype
     });
 }
 
+int montlok_model_predict_device_noalloc(const montlok_model* model, montlok_dtype dtype, const void* x,
+                                         size_t batch, double* out, void* stream) {
+    return guard([&] {
+        require(model != nullptr, "null model");
+        model->impl->predict_device_noalloc(input_type(dtype), x, batch, out, stream);
+    });
+}
+
 int montlok_model_predict_leaves(const montlok_model* model, montlok_dtype dtype, const void* x, size_t batch,
                                  int32_t* leaves) {
     return guard([&] {

@@ -119,6 +119,13 @@ public:
         return replicas_[device];
     }
 
+    // The replica on `device` if one was uploaded; never uploads (allocates).
+    const mlk_dev_forest* find(int device) {
+        std::lock_guard<std::mutex> lock(mu_);
+        if (device < 0 || static_cast<size_t>(device) >= replicas_.size()) return nullptr;
+        return replicas_[device];
+    }
+
 private:
     const ForestImage& img_;
     const Preprocess& pre_;
@@ -267,6 +274,27 @@ void Model::predict_device(InputType type, const void* x, size_t batch, double* 
     check_cuda(mlk_cuda_predict_device(devices_->on(current), static_cast<int>(type), x, batch, out, stream, err,
                                        sizeof err),
                err);
+}
+
+void Model::predict_device_noalloc(InputType type, const void* x, size_t batch, double* out, void* stream) const {
+    if (batch == 0) return;
+    check_call(type, x, out);
+    const size_t table = static_cast<size_t>(forest_->slots) * 32 * sizeof(int32_t);
+    if (table > mlk_cuda_noalloc_scratch_bytes()) {
+        fail(Status::Unsupported, "the model needs " + std::to_string(table) + " bytes of key table per 32 rows, more "
+                                  "than the " + std::to_string(mlk_cuda_noalloc_scratch_bytes()) +
+                                  "-byte scratch of the no-allocation path");
+    }
+    char err[kErr] = {0};
+    int current = 0;
+    check_cuda(mlk_cuda_current_device(&current, err, sizeof err), err);
+    const mlk_dev_forest* f = devices_->find(current);
+    if (!f) {
+        fail(Status::State, "the model is not resident on CUDA device " + std::to_string(current) +
+                                " yet: one montlok_model_predict or montlok_model_predict_device call there uploads it "
+                                "(those calls allocate), after which the no-allocation entry point can run");
+    }
+    check_cuda(mlk_cuda_predict_device_noalloc(f, static_cast<int>(type), x, batch, out, stream, err, sizeof err), err);
 }
 
 void Model::predict_leaves(InputType type, const void* x, size_t batch, int32_t* leaves, bool device,

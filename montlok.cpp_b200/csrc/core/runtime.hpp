@@ -175,6 +175,9 @@ public:
     void predict(InputType type, const void* x, size_t batch, double* out) const;
     // Device buffers on the current device, work queued on `stream`.
     void predict_device(InputType type, const void* x, size_t batch, double* out, void* stream) const;
+    // predict_device with no allocation at all (static scratch; the model
+    // must already be resident on the current device).
+    void predict_device_noalloc(InputType type, const void* x, size_t batch, double* out, void* stream) const;
     // Leaf node index of every (row, tree); host or device buffers.
     void predict_leaves(InputType type, const void* x, size_t batch, int32_t* leaves, bool device,
                         void* stream) const;

@@ -71,3 +71,8 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
                  std::string& err);
 
 }  // namespace mlk::cuda
+
+// The opaque handle of mlk_cuda.h: one device replica of a forest.
+struct mlk_dev_forest {
+    mlk::cuda::DevForest f;
+};

@@ -26,11 +26,14 @@
 // the input (exact_right).
 #include <algorithm>
 #include <climits>
+#include <cstring>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "device_common.cuh"
 #include "forest.cuh"
+#include "mlk_cuda.h"
 
 namespace mlk::cuda {
 namespace {
@@ -281,3 +284,120 @@ bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch
 }
 
 }  // namespace mlk::cuda
+
+// ---------------------------------------------------------------------------
+// Predicting without allocating (montlok_model_predict_device_noalloc).
+//
+// Some callers cannot allocate GPU memory while they predict: serving loops
+// whose device memory belongs to another allocator (a framework's caching
+// pool that has already reserved the GPU, so a cudaMalloc of ours would fail
+// or fragment it), and latency-critical paths that must not pay for
+// cudaMalloc/cudaFree or the device-wide synchronisation cudaFree implies.
+// For them this path runs the scratch-using variant of the generic kernel
+// (per-warp key tables [slot][32] int32 in global memory, normally obtained
+// per call) with its scratch in the fixed array below: 16 MiB, present on
+// every GPU that loads this library until the process exits. The grid is cut
+// to the warps whose tables fit; a model whose single 32-row table exceeds
+// the array (more than 131072 feature/missing-rule slots, about 32768
+// features) is rejected with MONTLOK_ERROR_UNSUPPORTED.
+//
+// On the host the array's name is only a stand-in, not a device address: the
+// first call on each device, with that device current, looks the real
+// address up with cudaGetSymbolAddress and caches it, so that first call
+// should come before any stream capture. All calls share the array; every
+// table is written in full by the kernel before it is read, so nothing needs
+// clearing between calls, but calls whose kernels overlap on the GPU (on
+// concurrent streams) race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t{16} << 20;
+}  // namespace
+
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+namespace mlk::cuda {
+namespace {
+
+// The device address of g_noalloc_scratch on `device`, looked up once.
+bool noalloc_scratch(int device, int** out, std::string& err) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, int*>> known;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& k : known) {
+        if (k.first == device) {
+            *out = k.second;
+            return true;
+        }
+    }
+    int previous = -1;
+    if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
+    if (previous != device && !check(cudaSetDevice(device), "cudaSetDevice", err)) return false;
+    int* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch);
+    if (previous >= 0 && previous != device) cudaSetDevice(previous);
+    if (!check(e, "cudaGetSymbolAddress", err)) return false;
+    known.emplace_back(device, p);
+    *out = p;
+    return true;
+}
+
+// 0 on success, else a montlok_status with `err` set.
+int launch_forest_noalloc(const DevForest& f, int dtype, const void* x, long long batch, double* out,
+                          cudaStream_t stream, std::string& err) {
+    if (batch <= 0) return 0;
+    const ForestArgs& a = f.args;
+    const size_t table = static_cast<size_t>(a.slots) * 32 * sizeof(int);
+    if (table > kNoAllocScratchBytes) {
+        err = "the model needs " + std::to_string(table) + " bytes of key table per 32 rows, more than the " +
+              std::to_string(kNoAllocScratchBytes) + "-byte scratch of the no-allocation path";
+        return 4;
+    }
+    int* scratch = nullptr;
+    if (!noalloc_scratch(f.device, &scratch, err)) return 7;
+    const long long fit = static_cast<long long>(kNoAllocScratchBytes / table);  // warps whose tables fit
+    const int wpc = fit >= 2 ? 2 : 1;
+    const long long groups = (batch + 31) / 32;
+    const long long want = std::min({(groups + wpc - 1) / wpc, fit / wpc, static_cast<long long>(f.sm_count) * 4});
+    const int grid = static_cast<int>(std::max<long long>(want, 1));
+    const int threads = 32 * wpc, smem = wpc * kStageBytes;
+    const bool ties = !a.cast_f32, f64 = dtype == 2;
+    const int kc_tmpl = a.K == 1 ? 1 : 8;
+    const bool softmax_after = a.link == 2 && a.K > kMaxOut;
+    for (int k0 = 0; k0 < a.K; k0 += kMaxOut) {
+        int kc = std::min(kMaxOut, a.K - k0);
+        int link_here = softmax_after ? 0 : 1;
+        int k0v = k0;
+        int* no_leaves = nullptr;
+        void* k = pick(ties, false, kc_tmpl, true, f64);
+        void* args[] = {const_cast<ForestArgs*>(&a), const_cast<void**>(&x), &batch, &out, &no_leaves, &k0v, &kc,
+                        &link_here, &scratch};
+        if (!check(cudaLaunchKernel(k, grid, threads, args, smem, stream), "no-allocation kernel launch", err)) {
+            return 7;
+        }
+    }
+    if (softmax_after) {
+        const int tpb = 128;
+        softmax_rows<<<static_cast<unsigned>((batch + tpb - 1) / tpb), tpb, 0, stream>>>(out, batch, a.K);
+        if (!check(cudaGetLastError(), "softmax kernel launch", err)) return 7;
+    }
+    return 0;
+}
+
+}  // namespace
+}  // namespace mlk::cuda
+
+extern "C" size_t mlk_cuda_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int mlk_cuda_predict_device_noalloc(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch,
+                                               double* out, void* stream, char* err, size_t errlen) {
+    std::string e;
+    const int status = mlk::cuda::launch_forest_noalloc(forest->f, dtype, x, static_cast<long long>(batch), out,
+                                                        static_cast<cudaStream_t>(stream), e);
+    if (status != 0 && err && errlen) {
+        const size_t n = std::min(errlen - 1, e.size());
+        std::memcpy(err, e.data(), n);
+        err[n] = '\0';
+    }
+    return status;
+}

@@ -71,6 +71,13 @@ int mlk_cuda_predict_device(const mlk_dev_forest* forest, int dtype, const void*
                             void* stream, char* err, size_t errlen);
 int mlk_cuda_leaves_device(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,
                            void* stream, char* err, size_t errlen);
+/* predict_device without any allocation: the key tables live in a static
+ * device array of this library (forest_kernels.cu), whose size
+ * mlk_cuda_noalloc_scratch_bytes() gives. Returns 4
+ * (MONTLOK_ERROR_UNSUPPORTED) when one 32-row key table exceeds it. */
+size_t mlk_cuda_noalloc_scratch_bytes(void);
+int mlk_cuda_predict_device_noalloc(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch,
+                                    double* out, void* stream, char* err, size_t errlen);
 int mlk_cuda_predict_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
                           char* err, size_t errlen);
 int mlk_cuda_leaves_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,

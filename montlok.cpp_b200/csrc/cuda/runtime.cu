@@ -288,10 +288,6 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
 }  // namespace
 }  // namespace mlk::cuda
 
-struct mlk_dev_forest {
-    mlk::cuda::DevForest f;
-};
-
 using mlk::cuda::DevForest;
 using mlk::cuda::put_error;
 
