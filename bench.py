@@ -54,7 +54,7 @@ def peaks() -> tuple[float, str]:
 
 def traffic_per_launch(config: str) -> float | None:
     """DRAM bytes per launch of the predict kernel from the committed ncu summary."""
-    path = ROOT / "profiles" / f"forest_kernel_{config}_traffic.json"
+    path = ROOT / "profiles" / f"{config}_dram_traffic.json"
     if not path.exists():
         return None
     return float(json.loads(path.read_text())["dram_bytes_per_launch"])
