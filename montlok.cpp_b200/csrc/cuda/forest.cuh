@@ -33,7 +33,9 @@ struct ForestArgs {
 // Complete-tree layout (heap_kernels.cu); depth 0 when the model has none.
 struct HeapArgs {
     int depth, rows, leaf32, buffers;
+    int slot_bits;               // low bits of a split word holding the slot
     const unsigned char* trees;  // whole chunks of heap_record_bytes(depth, leaf32) records, inert trees last
+    const int* tfull;            // [padded trees * (2^depth - 1)]: full threshold key of each split
     const int* node_ids;         // [T * (2^depth - 1)]: file node of each heap split, -1 for padding
     int* status;
 };
@@ -67,6 +69,7 @@ bool prepare_kernels(const DevForest& f, std::string& err);
 bool heap_plan(int slots, int depth, bool leaf32, int& rows, int& buffers);
 int heap_record_bytes(int depth, bool leaf32);
 int heap_chunk_trees();
+int heap_slot_bits(int slots);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
 

@@ -1,31 +1,41 @@
 // Complete-tree predict kernel for sm_100a (depth <= 8, one output).
 //
-// Every tree is stored as a complete binary tree of depth D in heap order
-// (children of split i at 2i+1 and 2i+2; shallower leaves are padded with
-// always-left splits), one 16-byte aligned record per tree: 2^D - 1 splits of
-// 8 bytes (threshold key T, byte offset of the split's slot in the key table)
-// followed by 2^D leaf values (float32 when every leaf is exactly a float,
-// else float64). Child addresses are implicit, so a step is: one 8-byte
-// shared load of the split, one shared load of the row's key, one compare,
-// and new address = 2 * address + (8 or 16) - base.
+// Tree record. Every tree is stored as a complete binary tree of depth D in
+// heap order (children of split i at 2i+1 and 2i+2; shallower leaves are
+// padded with always-left splits), one 16-byte aligned record per tree:
+// 2^D split words of 4 bytes (the last one unused, so the leaves start 8-byte
+// aligned) and 2^D leaf values (float32 when every leaf is exactly a float,
+// else float64). A split word packs the threshold key and the slot:
 //
-// A CTA owns R rows for the whole ensemble and runs two teams of R threads
-// (one thread per row in each). The rows' key tables stay in shared memory
-// ([slot][R] int32, lane l always reading bank l). Trees stream through a ring
-// of four chunk buffers (kChunk trees each; chunk c of every row group uses
-// buffer c % 4) filled by one-dimensional bulk async copies (cp.async.bulk,
-// completion counted on one mbarrier per buffer): while team 0 walks chunk
-// 2p and team 1 walks chunk 2p + 1, the copies of chunks 2p + 2 and 2p + 3
-// are in flight. Team 1 hands the leaf it reached in each tree to team 0
-// through a small shared exchange, and team 0 adds every leaf value in tree
-// order, so the float64 sums are the reference's (trees.cpp:366-388): a chunk
-// never straddles a block of 64 trees, block 0 adds onto the base score,
-// later blocks sum from 0.0 and are added when they end.
+//     word = (T & ~mask) | slot          mask = 2^slot_bits - 1
 //
-// The device tree array is padded with inert trees to whole chunks, so every
-// copy is a full chunk and no walk ever reads an unwritten buffer. Waits on
-// the mbarriers are bounded; on timeout the kernel records an error in the
-// forest's status word, waits (bounded) for its copies in flight, and stops.
+// so a step compares the row's key k against the threshold's high bits:
+// k > (word | mask) proves k > T and k < (word & ~mask) proves k <= T. When
+// k and T agree in those high bits (a float32 within a relative 2^-(23 -
+// slot_bits) of the threshold: rare), the split is decided exactly from the
+// full threshold key kept in a global array, and for float64 models on a
+// full-key tie from the doubles, as the generic kernel does.
+//
+// Work split. A CTA owns R rows for the whole ensemble: their key tables
+// ([slot][R] int32, lane l always reading bank l) stay in shared memory. Four
+// teams of R threads (one thread per row in each) walk disjoint 64-tree
+// blocks: team j takes blocks j, j + 4, j + 8, ... Blocks are what the
+// reference sums separately (trees.cpp:366-388: block 0 onto the base score,
+// every later block from 0.0, then the blocks in order), so a team adds its
+// leaves in tree order into its own block partial and never waits for another
+// team inside a block. After each round of four blocks the partials meet in
+// shared memory (one CTA barrier) and team 0 adds them to the row's sum in
+// block order, which reproduces the reference's float64 association exactly.
+//
+// Streaming. Each team streams its trees through a private pair of chunk
+// buffers (4 trees each, one thread walking the 4 side by side), filled by
+// one-dimensional bulk async copies (cp.async.bulk) whose completion counts on
+// one mbarrier per buffer; a team barrier (named barrier j + 1) releases a
+// buffer and the team's first thread refills it two chunks ahead. The device
+// tree array is padded with inert trees to whole chunks, so every copy is a
+// full chunk. Waits are bounded: on timeout the kernel records an error in the
+// forest's status word, waits (bounded) for its own copies in flight, and
+// every thread of the CTA leaves together.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -37,35 +47,39 @@
 namespace mlk::cuda {
 namespace {
 
-constexpr int kChunk = 8;    // trees per streamed chunk = trees one thread walks side by side
-constexpr int kBuffers = 4;  // chunk buffers: two walked, two in flight
-static_assert(kTreeBlock % kChunk == 0, "chunks never straddle a block of 64 trees");
-constexpr int kTile = 16;                         // features per transpose tile
-constexpr int kTileBytes = 32 * (kTile + 1) * 8;  // one warp's transpose tile
-constexpr long long kSpinLimit = 1ll << 26;       // mbarrier polls before giving up
+constexpr int kTeams = 4;                              // teams of R threads, one 64-tree block each at a time
+constexpr int kTrees = 4;                              // trees per chunk = trees one thread walks side by side
+constexpr int kChunksPerBlock = kTreeBlock / kTrees;   // 16
+constexpr int kTile = 4;                               // features per transpose tile in the prepare
+constexpr int kTileBytes = 32 * (kTile + 1) * 8;       // one warp's transpose tile
+constexpr long long kSpinLimit = 1ll << 26;            // mbarrier polls before giving up
 constexpr int kHeapSmemLimit = 227 * 1024;
+constexpr int kMaxSlotBits = 10;
+static_assert(kTreeBlock % kTrees == 0, "chunks never straddle a block of 64 trees");
 
-__host__ __device__ constexpr int heap_tree_bytes(int depth, bool leaf32) {
-    return (((1 << depth) - 1) * 8 + (1 << depth) * (leaf32 ? 4 : 8) + 15) & ~15;
+__host__ __device__ constexpr int record_bytes(int depth, bool leaf32) {
+    return ((4 << depth) + (1 << depth) * (leaf32 ? 4 : 8) + 15) & ~15;
 }
 
 __host__ __device__ constexpr int align128(int n) { return (n + 127) & ~127; }
 
-// Shared memory layout (byte offsets): barriers at 0 | keys [slots][R] int32
-// | exchange [kChunk][R] u8 | ring of four chunk buffers; during the prepare
-// phase the ring past buffer 1 holds the transpose tiles.
+// Shared memory layout (byte offsets): mbarriers [team][2] at 0 | keys
+// [slots][R] int32 | block partials [2][team][R] double | first buffers of
+// the four teams | second buffers of the four teams. During the prepare the
+// second buffers (not yet refilled) hold the warps' transpose tiles.
 struct Layout {
-    int keys, exchange, ring, total;
+    int keys, parts, ring0, ring1, total;
 };
 
 __host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, int rows) {
     Layout l{};
     l.keys = 128;
-    l.exchange = l.keys + align128(slots * rows * 4);
-    l.ring = l.exchange + align128(kChunk * rows);
-    const int chunk = kChunk * heap_tree_bytes(depth, leaf32);
-    const int tiles = 2 * (rows / 32) * kTileBytes;  // every warp of both teams prepares
-    l.total = l.ring + align128(max(kBuffers * chunk, 2 * chunk + tiles));
+    l.parts = l.keys + align128(slots * rows * 4);
+    l.ring0 = l.parts + align128(2 * kTeams * rows * 8);
+    const int chunk = kTrees * record_bytes(depth, leaf32);
+    l.ring1 = l.ring0 + align128(kTeams * chunk);
+    const int tiles = kTeams * (rows / 32) * kTileBytes;
+    l.total = l.ring1 + align128(max(kTeams * chunk, tiles));
     return l;
 }
 
@@ -77,12 +91,11 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Thread 0: arm the barrier for `bytes` and start the copy global -> shared.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+// Arms `bar` for `bytes` and starts the copy global -> shared (one thread).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
@@ -101,10 +114,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
-// Shared-memory loads at explicit 32-bit shared addresses.
-__device__ __forceinline__ int2 lds_v2(uint32_t a) {
-    int2 v;
-    asm volatile("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+// Named barrier `id` over `threads` threads that also ORs `v` across them.
+__device__ __forceinline__ bool team_sync_or(int id, int threads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, %2, %3, p; selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
     return v;
 }
 __device__ __forceinline__ int lds_s32(uint32_t a) {
@@ -133,68 +156,154 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
     }
 }
 
-// Walks the kChunk trees of the chunk at shared address `buf` for one row;
-// leaf[t] receives the index (0 .. 2^D - 1) of the leaf reached in tree t.
-template <int D, bool TIES, typename XT>
-__device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
-                                           int chunk, int live, const XT* x, long long row, long long batch,
-                                           uint32_t (&leaf)[kChunk], int tree_bytes) {
-    constexpr int kSplits = (1 << D) - 1;
-    uint32_t p[kChunk], go_left[kChunk], go_right[kChunk];
+// Keys of the 32 rows row0 .. row0 + 31 for features [f_begin, f_end): the
+// warp reads kTile features of all 32 rows per step (four coalesced loads of
+// 8 rows x kTile values, the next step's loads in flight meanwhile), stages
+// them in `tile` ([32][kTile + 1] doubles) and each lane turns its own row's
+// values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
+template <int STRIDE, typename XT>
+__device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
+                             double* tile, int lane, int f_begin, int f_end) {
+    constexpr int kPerLoad = 32 / kTile;  // rows covered by one warp-wide load
+    const int sub = lane / kTile, f_in = lane % kTile;
+    double raw[kTile], next[kTile];
+    auto load = [&](int f0, double (&v)[kTile]) {
+        const int feat = f0 + f_in;
 #pragma unroll
-    for (int t = 0; t < kChunk; ++t) {
-        p[t] = buf + t * tree_bytes;
-        go_left[t] = 8u - p[t];
-        go_right[t] = 16u - p[t];
+        for (int i = 0; i < kTile; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            v[i] = (feat < f_end && row < batch) ? load_x(x + row * a.F + feat) : 0.0;
+        }
+    };
+    if (f_begin < f_end) load(f_begin, raw);
+    for (int f0 = f_begin; f0 < f_end; f0 += kTile) {
+        if (f0 + kTile < f_end) load(f0 + kTile, next);
+        const int feat = f0 + f_in;
+        double mean = 0.0, scale = 1.0;
+        if (a.standardize && feat < f_end) {
+            mean = __ldg(a.pre_mean + feat);
+            scale = __ldg(a.pre_scale + feat);
+        }
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            tile[(i * kPerLoad + sub) * (kTile + 1) + f_in] =
+                (feat < f_end && row < batch) ? finish(a, raw[i], mean, scale) : 0.0;
+        }
+        __syncwarp();
+        const int nf = min(kTile, f_end - f0);
+        for (int j = 0; j < nf; ++j) {
+            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kTile + 1) + j]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) raw[i] = next[i];
     }
+}
+
+// The exact decision of a split whose packed word tied with the row's key:
+// the full threshold key, then (float64 models, equal keys) the doubles.
+template <bool TIES, typename XT>
+__device__ __noinline__ bool tied_right(const ForestArgs& a, const HeapArgs& h, const XT* __restrict__ x, long long row,
+                                        long long batch, int key, int tree, int split, bool live) {
+    const int splits = (1 << h.depth) - 1;
+    const int t = __ldg(h.tfull + static_cast<size_t>(tree) * splits + split);
+    if (TIES && live && key == t) {
+        return exact_right(a, x, row, batch, __ldg(h.node_ids + static_cast<size_t>(tree) * splits + split));
+    }
+    return key > t;
+}
+
+// Walks the kTrees trees of the chunk at shared address `buf` for one row and
+// adds the leaves of the first `live` of them, in order, to `part`.
+template <int D, int R, bool LEAF32, bool TIES, typename XT>
+__device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
+                                           uint32_t mask, int chunk, int live, const XT* x, long long row,
+                                           long long batch, double& part) {
+    constexpr int kSplits = (1 << D) - 1;
+    constexpr int kRec = record_bytes(D, LEAF32);
+    constexpr int kLeafBytes = LEAF32 ? 4 : 8;
+    constexpr int kShift = R == 128 ? 9 : (R == 64 ? 8 : 7);  // log2(R * 4): bytes of one slot's column
+    static_assert(R == 128 || R == 64 || R == 32, "rows per CTA");
+    uint32_t p[kTrees];
+#pragma unroll
+    for (int t = 0; t < kTrees; ++t) p[t] = buf + t * kRec;
 #pragma unroll
     for (int d = 0; d < D; ++d) {
-        int2 n[kChunk];
-        int kv[kChunk];
+        uint32_t n[kTrees];
+        int k[kTrees];
+        bool right[kTrees];
 #pragma unroll
-        for (int t = 0; t < kChunk; ++t) n[t] = lds_v2(p[t]);
+        for (int t = 0; t < kTrees; ++t) n[t] = lds_u32(p[t]);
 #pragma unroll
-        for (int t = 0; t < kChunk; ++t) kv[t] = lds_s32(col + n[t].y);
+        for (int t = 0; t < kTrees; ++t) k[t] = lds_s32(col + ((n[t] & mask) << kShift));
+        bool tie = false;
 #pragma unroll
-        for (int t = 0; t < kChunk; ++t) {
-            bool right = kv[t] > n[t].x;
-            if (TIES && kv[t] == n[t].x && t < live) {
-                const uint32_t base = buf + t * tree_bytes;
-                const int node = __ldg(h.node_ids + static_cast<size_t>(chunk * kChunk + t) * kSplits +
-                                       ((p[t] - base) >> 3));
-                right = exact_right(a, x, row, batch, node);
+        for (int t = 0; t < kTrees; ++t) {
+            right[t] = k[t] > static_cast<int>(n[t] | mask);
+            tie |= static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask;
+        }
+        if (__any_sync(0xffffffffu, tie)) {
+#pragma unroll
+            for (int t = 0; t < kTrees; ++t) {
+                if (static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask) {
+                    const uint32_t base = buf + t * kRec;
+                    right[t] = tied_right<TIES>(a, h, x, row, batch, k[t], chunk * kTrees + t,
+                                                static_cast<int>((p[t] - base) >> 2), t < live);
+                }
             }
-            p[t] = 2 * p[t] + (right ? go_right[t] : go_left[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < kTrees; ++t) {
+            const uint32_t base = buf + t * kRec;
+            p[t] = 2 * p[t] - base + (right[t] ? 8u : 4u);
         }
     }
 #pragma unroll
-    for (int t = 0; t < kChunk; ++t) leaf[t] = ((p[t] - (buf + t * tree_bytes)) >> 3) - kSplits;
+    for (int t = 0; t < kTrees; ++t) {
+        if (t < live) {
+            const uint32_t base = buf + t * kRec;
+            const uint32_t leaf = ((p[t] - base) >> 2) - kSplits;
+            part = __dadd_rn(part, lds_leaf(base + (4u << D) + leaf * kLeafBytes, LEAF32));
+        }
+    }
 }
 
 template <int D, int R, bool LEAF32, bool TIES, typename XT>
-__global__ void __launch_bounds__(2 * R) heap_kernel(const ForestArgs a, const HeapArgs h, const XT* __restrict__ x,
-                                                     long long batch, double* __restrict__ out) {
-    constexpr int kSplits = (1 << D) - 1;
-    constexpr int kTreeBytes = heap_tree_bytes(D, LEAF32);
-    constexpr int kChunkBytes = kChunk * kTreeBytes;
-    constexpr int kLeafBytes = LEAF32 ? 4 : 8;
+__global__ void __launch_bounds__(kTeams * R) heap_kernel(const ForestArgs a, const HeapArgs h,
+                                                          const XT* __restrict__ x, long long batch,
+                                                          double* __restrict__ out) {
+    constexpr int kChunkBytes = kTrees * record_bytes(D, LEAF32);
+    constexpr int kWarpsPerTeam = R / 32;
     extern __shared__ __align__(128) unsigned char smem[];
     const Layout L = layout_of(a.slots, D, LEAF32, R);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [team][buffer]
     int* keys = reinterpret_cast<int*>(smem + L.keys);
-    unsigned char* exchange = smem + L.exchange;
-    unsigned char* ring = smem + L.ring;
-    const uint32_t ring0 = smem_u32(ring);
+    double* parts = reinterpret_cast<double*>(smem + L.parts);
 
     const int tid = threadIdx.x;
-    const int team = tid / R, r = tid % R;  // team 0 walks chunk 2p, team 1 chunk 2p + 1
+    const int team = tid / R, r = tid % R;
     const int warp = tid >> 5, lane = tid & 31;
-    const int chunks = (a.T + kChunk - 1) / kChunk;
-    const int pairs = (chunks + 1) / 2;
+    const bool producer = r == 0;  // issues the team's copies
+    const int chunks = (a.T + kTrees - 1) / kTrees;
+    const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
+    const int rounds = (blocks + kTeams - 1) / kTeams;
     const long long groups = (batch + R - 1) / R;
     const size_t row_bytes = static_cast<size_t>(a.F) * sizeof(XT);
+    const uint32_t mask = (1u << h.slot_bits) - 1u;
+    // The team's chunks in walking order: blocks team, team + 4, ...; the
+    // q-th is chunk_at(q), and n_team of them per row group.
+    int n_team = 0;
+    for (int b = team; b < blocks; b += kTeams) n_team += min(kChunksPerBlock, chunks - b * kChunksPerBlock);
+    auto chunk_at = [&](int q) {
+        return (team + kTeams * (q / kChunksPerBlock)) * kChunksPerBlock + q % kChunksPerBlock;
+    };
+    const uint32_t buf0 = smem_u32(smem + L.ring0) + team * kChunkBytes;
+    const uint32_t buf1 = smem_u32(smem + L.ring1) + team * kChunkBytes;
+    uint64_t* team_bar = bar + 2 * team;
+
     if (tid == 0) {
-        for (int b = 0; b < kBuffers; ++b) mbar_init(&bar[b]);
+        for (int b = 0; b < 2 * kTeams; ++b) mbar_init(&bar[b]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (blockIdx.x < groups) {
             const long long r0 = static_cast<long long>(blockIdx.x) * R;
@@ -203,119 +312,93 @@ __global__ void __launch_bounds__(2 * R) heap_kernel(const ForestArgs a, const H
     }
     __syncthreads();
 
-    // Chunk c of the CTA's k-th row group goes to buffer c % 4 and completes
-    // that buffer's barrier for the (k * per_buffer(b) + c / 4)-th time, whose
-    // parity is what a wait names. Thread 0 remembers the parity of the last
-    // copy it issued to each buffer, so a failing CTA can wait out whatever is
-    // still in flight before it exits.
-    auto parity_of = [&](unsigned k, int c) -> uint32_t {
-        const unsigned b = static_cast<unsigned>(c) & 3u;
-        const unsigned per_buffer = (static_cast<unsigned>(chunks) + 3u - b) / 4u;
-        return (k * per_buffer + static_cast<unsigned>(c >> 2)) & 1u;
+    // Buffer b's k-th fill completes its barrier's phase k: every thread of
+    // the team counts the fills it has consumed, the producer those it issued
+    // (to wait out copies in flight before an early exit).
+    uint32_t consumed[2] = {0u, 0u}, issued[2] = {0u, 0u};
+    auto issue = [&](int q) {
+        const int b = q & 1;
+        bulk_load(b ? buf1 : buf0, h.trees + static_cast<size_t>(chunk_at(q)) * kChunkBytes, kChunkBytes,
+                  &team_bar[b]);
+        ++issued[b];
     };
-    uint32_t issued_mask = 0, issued_parity = 0;
-    unsigned k = 0;  // row groups this CTA has started
-    auto issue = [&](int c) {
-        const unsigned b = static_cast<unsigned>(c) & 3u;
-        bulk_load(ring + b * kChunkBytes, h.trees + static_cast<size_t>(c) * kChunkBytes, kChunkBytes, &bar[b]);
-        issued_mask |= 1u << b;
-        issued_parity = (issued_parity & ~(1u << b)) | (parity_of(k, c) << b);
-    };
+    if (producer && n_team > 0 && blockIdx.x < groups) issue(0);
 
     const uint32_t col = smem_u32(keys) + r * 4;  // this row's key column
-    for (long long g = blockIdx.x; g < groups; g += gridDim.x, ++k) {
+    for (long long g = blockIdx.x; g < groups; g += gridDim.x) {
         const long long row0 = g * R;
         const long long row = row0 + r;
-        if (tid == 0) {
-            for (int c = 0; c < min(chunks, 2); ++c) issue(c);
-        }
-        // Prepare: warp w builds the keys of rows 32 (w % (R / 32)) .. + 31,
-        // team 0 for the first half of the features and team 1 for the rest,
-        // with its transpose tile in the ring past buffer 1 (free until the
-        // copies of chunks 2 and 3 start below).
         {
-            const int wr = warp % (R / 32);
-            const int half = (a.F + 1) / 2;
-            double* tile = reinterpret_cast<double*>(ring + 2 * kChunkBytes + warp * kTileBytes);
-            prepare_group<R, kTile>(a, x, row0 + wr * 32, batch, keys + wr * 32, tile, lane, team ? half : 0,
-                                    team ? a.F : half, team == 0);
+            // Prepare: warp w builds the keys of rows 32 (w % (R / 32)) .. + 31
+            // for the team's quarter of the features.
+            const int slice = warp % kWarpsPerTeam;
+            const int per = (a.F + kTeams - 1) / kTeams;
+            const int f_begin = min(a.F, team * per), f_end = min(a.F, f_begin + per);
+            double* tile = reinterpret_cast<double*>(smem + L.ring1 + warp * kTileBytes);
+            prepare_rows<R>(a, x, row0 + slice * 32, batch, keys + slice * 32, tile, lane, f_begin, f_end);
+            if (team == 0) keys[a.pad_slot * R + slice * 32 + lane] = INT_MIN;
         }
         __syncthreads();
-        if (tid == 0) {
-            for (int c = 2; c < min(chunks, 4); ++c) issue(c);
-            if (g + gridDim.x < groups) {  // the next group's rows into L2 while this one walks
-                const long long r1 = row0 + static_cast<long long>(gridDim.x) * R;
-                prefetch_l2(x + r1 * a.F, static_cast<size_t>(min(static_cast<long long>(R), batch - r1)) * row_bytes);
-            }
+        if (producer && n_team > 1) issue(1);
+        if (tid == 0 && g + gridDim.x < groups) {  // the next group's rows into L2 while this one walks
+            const long long r1 = row0 + static_cast<long long>(gridDim.x) * R;
+            prefetch_l2(x + r1 * a.F, static_cast<size_t>(min(static_cast<long long>(R), batch - r1)) * row_bytes);
         }
-        double acc = a.mean ? 0.0 : __ldg(a.base);
-        double part = 0.0;
-        bool bad = false;  // this thread's wait timed out; decided CTA-wide at the next barrier
 
-        // Adds the leaves of chunk c (indices in leaf[]) in tree order.
-        auto add_chunk = [&](int c, const uint32_t (&leaf)[kChunk]) {
-            const uint32_t buf = ring0 + (static_cast<unsigned>(c) & 3u) * kChunkBytes;
-            const int live = min(kChunk, a.T - c * kChunk);
-            const bool first_block = c * kChunk < kTreeBlock;
-            if (!first_block && (c * kChunk) % kTreeBlock == 0) {
-                // A block of 64 trees ended with the previous chunk.
-                if (c * kChunk >= 2 * kTreeBlock) acc = __dadd_rn(acc, part);
-                part = 0.0;
-            }
-#pragma unroll
-            for (int t = 0; t < kChunk; ++t) {
-                if (t < live) {
-                    const double v = lds_leaf(buf + t * kTreeBytes + kSplits * 8 + leaf[t] * kLeafBytes, LEAF32);
-                    if (first_block) acc = __dadd_rn(acc, v);
-                    else part = __dadd_rn(part, v);
+        double acc = 0.0;  // team 0: the row's sum over the rounds done
+        bool bad = false;  // a wait of this team timed out (team-uniform)
+        int q = 0;         // position in the team's chunk list
+        for (int k = 0; k < rounds; ++k) {
+            const int block = team + kTeams * k;
+            if (block < blocks && !bad) {
+                const int c0 = block * kChunksPerBlock;
+                const int cn = min(kChunksPerBlock, chunks - c0);
+                double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+                for (int c = 0; c < cn; ++c, ++q) {
+                    const int b = q & 1;
+                    // Warp-uniform: the walk's votes need every lane.
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u));
+                    ++consumed[b];
+                    if (ok) {
+                        walk_chunk<D, R, LEAF32, TIES>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
+                                                       min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
+                    }
+                    // Every thread of the team is done with buffer b.
+                    if (team_sync_or(team + 1, R, !ok)) {
+                        bad = true;
+                        break;
+                    }
+                    if (producer && q + 2 < n_team) issue(q + 2);
                 }
+                parts[((k & 1) * kTeams + team) * R + r] = part;
             }
-        };
-
-        for (int pr = 0; pr < pairs; ++pr) {
-            if (pr > 0) {
-                if (__syncthreads_or(bad)) break;  // pair pr - 1 is done: its buffers take pair pr + 1
-                if (tid == 0) {
-                    for (int c = 2 * pr + 2; c < min(chunks, 2 * pr + 4); ++c) issue(c);
-                }
+            if (__syncthreads_or(bad)) {
+                bad = true;
+                break;
             }
-            const int mine = 2 * pr + team;
-            uint32_t leaf[kChunk];
-            if (mine < chunks) {
-                if (!mbar_wait(&bar[mine & 3], parity_of(k, mine))) {
-                    bad = true;
-                } else {
-                    const uint32_t buf = ring0 + (static_cast<unsigned>(mine) & 3u) * kChunkBytes;
-                    walk_chunk<D, TIES>(a, h, buf, col, mine, min(kChunk, a.T - mine * kChunk), x, row, batch, leaf,
-                                        kTreeBytes);
-                    if (team == 0) {
-                        add_chunk(mine, leaf);
-                    } else {
+            if (team == 0) {
 #pragma unroll
-                        for (int t = 0; t < kChunk; ++t) exchange[t * R + r] = static_cast<unsigned char>(leaf[t]);
+                for (int j = 0; j < kTeams; ++j) {
+                    const int blk = kTeams * k + j;
+                    if (blk < blocks) {
+                        const double v = parts[((k & 1) * kTeams + j) * R + r];
+                        acc = blk == 0 ? v : __dadd_rn(acc, v);
                     }
                 }
             }
-            if (__syncthreads_or(bad)) break;  // team 1's leaves are in the exchange
-            if (team == 0 && mine + 1 < chunks) {
-#pragma unroll
-                for (int t = 0; t < kChunk; ++t) leaf[t] = exchange[t * R + r];
-                add_chunk(mine + 1, leaf);
-            }
         }
-        if (__syncthreads_or(bad)) {
+        if (bad) {
             // Leave no bulk copy in flight into shared memory: wait (bounded)
             // for the last copy issued to each buffer, then stop.
-            if (tid == 0) {
-                atomicExch(h.status, 1);
-                for (int b = 0; b < kBuffers; ++b) {
-                    if (issued_mask & (1u << b)) mbar_wait(&bar[b], (issued_parity >> b) & 1u);
+            if (producer) {
+                if (team == 0) atomicExch(h.status, 1);
+                for (int b = 0; b < 2; ++b) {
+                    if (issued[b] > 0) mbar_wait(&team_bar[b], (issued[b] - 1u) & 1u);
                 }
             }
             return;
         }
         if (team == 0 && row < batch) {
-            if (a.T > kTreeBlock) acc = __dadd_rn(acc, part);
             double v[1] = {acc};
             if (a.mean) {
                 const int n = __ldg(a.counts);
@@ -324,7 +407,10 @@ __global__ void __launch_bounds__(2 * R) heap_kernel(const ForestArgs a, const H
             apply_link<1>(a, v, 1);
             out[row] = v[0];
         }
-        __syncthreads();  // keys, exchange and buffers are rewritten by the next group
+        // Every team passed the last round's barrier, so the buffers and tiles
+        // are free: start the next group's first chunk.
+        if (producer && n_team > 0 && g + gridDim.x < groups) issue(0);
+        __syncthreads();  // keys and partials are rewritten by the next group
     }
 }
 
@@ -369,17 +455,25 @@ void* pick_heap(int depth, int rows, bool leaf32, bool ties, bool f64) {
 
 }  // namespace
 
-int heap_record_bytes(int depth, bool leaf32) { return heap_tree_bytes(depth, leaf32); }
+int heap_record_bytes(int depth, bool leaf32) { return record_bytes(depth, leaf32); }
 
-int heap_chunk_trees() { return kChunk; }
+int heap_chunk_trees() { return kTrees; }
 
-// The most rows per CTA (128, 64, 32) whose key tables and ring fit.
+int heap_slot_bits(int slots) {
+    int bits = 1;
+    while ((1 << bits) < slots) ++bits;
+    return bits;
+}
+
+// The most rows per CTA (128, 64, 32) whose key tables, partials and team
+// buffers fit; false when none do or the slot index needs more than
+// kMaxSlotBits bits of the split word.
 bool heap_plan(int slots, int depth, bool leaf32, int& rows, int& buffers) {
-    if (depth < 1 || depth > 8) return false;
+    if (depth < 1 || depth > 8 || heap_slot_bits(slots) > kMaxSlotBits) return false;
     for (int r : {128, 64, 32}) {
         if (layout_of(slots, depth, leaf32, r).total <= kHeapSmemLimit) {
             rows = r;
-            buffers = kBuffers;
+            buffers = 2;
             return true;
         }
     }
@@ -415,7 +509,7 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
     ForestArgs a = f.args;
     HeapArgs hh = h;
     void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out};
-    const cudaError_t e = cudaLaunchKernel(k, grid, 2 * h.rows, args, smem, stream);
+    const cudaError_t e = cudaLaunchKernel(k, grid, kTeams * h.rows, args, smem, stream);
     if (e != cudaSuccess) {
         err = std::string("complete-tree kernel launch: ") + cudaGetErrorString(e);
         return false;

@@ -426,47 +426,55 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     f.status_host = static_cast<int*>(status);
     *f.status_host = 0;
     f.heap.status = a.status;
-    // Complete-tree records: [2^d - 1 splits (T, slot)] [2^d leaves], 16-byte aligned.
+    // Complete-tree records: [2^d split words, the last unused] [2^d leaves],
+    // 16-byte aligned; a split word is (T & ~mask) | slot.
     const int D = v->complete_depth;
     int rows = 0, buffers = 0;
-    if (D > 0 && heap_plan(v->slots, D, v->heap_leaf_f32 != 0, rows, buffers)) {
+    if (D > 0 && T > 0 && heap_plan(v->slots, D, v->heap_leaf_f32 != 0, rows, buffers)) {
         const bool f32 = v->heap_leaf_f32 != 0;
         const size_t splits = (size_t{1} << D) - 1, leaves = size_t{1} << D;
         const size_t rec = static_cast<size_t>(heap_record_bytes(D, f32));
+        const int slot_bits = heap_slot_bits(v->slots);
+        const uint32_t mask = (1u << slot_bits) - 1u;
         // Whole chunks: the tail is inert trees (every split goes left, to
         // leaves of 0.0), which the kernel walks but never adds.
         const size_t chunk = static_cast<size_t>(heap_chunk_trees());
         const size_t padded = (T + chunk - 1) / chunk * chunk;
         std::vector<unsigned char> host(padded * rec, 0);
+        std::vector<int32_t> full(padded * splits, INT32_MAX);
         for (size_t t = 0; t < padded; ++t) {
-            // The kernel reads a split's second word as the byte offset of its
-            // slot in the [slot][rows] key table.
-            int32_t* w = reinterpret_cast<int32_t*>(host.data() + t * rec);
+            uint32_t* w = reinterpret_cast<uint32_t*>(host.data() + t * rec);
             const int32_t* src = t < T ? v->heap_words + t * splits * 2 : nullptr;
             for (size_t i = 0; i < splits; ++i) {
-                w[2 * i] = src ? src[2 * i] : INT32_MAX;
-                w[2 * i + 1] = (src ? src[2 * i + 1] : v->pad_slot) * rows * 4;
+                const int32_t thr = src ? src[2 * i] : INT32_MAX;
+                const int32_t slot = src ? src[2 * i + 1] : v->pad_slot;
+                w[i] = (static_cast<uint32_t>(thr) & ~mask) | static_cast<uint32_t>(slot);
+                full[t * splits + i] = thr;
             }
         }
         for (size_t t = 0; t < T; ++t) {
-            unsigned char* r = host.data() + t * rec;
+            unsigned char* r = host.data() + t * rec + (size_t{4} << D);
             for (size_t j = 0; j < leaves; ++j) {
                 const double value = v->heap_leaf[t * leaves + j];
                 if (f32) {
                     const float fv = static_cast<float>(value);
-                    std::memcpy(r + splits * 8 + j * 4, &fv, 4);
+                    std::memcpy(r + j * 4, &fv, 4);
                 } else {
-                    std::memcpy(r + splits * 8 + j * 8, &value, 8);
+                    std::memcpy(r + j * 8, &value, 8);
                 }
             }
         }
         void* trees = nullptr;
         void* ids = nullptr;
+        void* tfull = nullptr;
         if (!device_alloc(&trees, host.size(), e) ||
             !ok(cudaMemcpy(trees, host.data(), host.size(), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+            !device_alloc(&tfull, full.size() * 4, e) ||
+            !ok(cudaMemcpy(tfull, full.data(), full.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
             !device_alloc(&ids, T * splits * 4, e) ||
             !ok(cudaMemcpy(ids, v->heap_node_id, T * splits * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
             if (trees) cudaFree(trees);
+            if (tfull) cudaFree(tfull);
             if (ids) cudaFree(ids);
             cudaFreeHost(status);
             cudaFree(block);
@@ -474,12 +482,15 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
             return kInternal;
         }
         f.blocks[f.nblocks++] = trees;
+        f.blocks[f.nblocks++] = tfull;
         f.blocks[f.nblocks++] = ids;
         f.heap.depth = D;
         f.heap.rows = rows;
         f.heap.buffers = buffers;
         f.heap.leaf32 = f32;
+        f.heap.slot_bits = slot_bits;
         f.heap.trees = static_cast<const unsigned char*>(trees);
+        f.heap.tfull = static_cast<const int*>(tfull);
         f.heap.node_ids = static_cast<const int*>(ids);
     }
     if (!prepare_kernels(f, e)) {
