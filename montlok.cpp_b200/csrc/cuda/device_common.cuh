@@ -40,10 +40,13 @@ __device__ __forceinline__ double finish(const ForestArgs& a, double v, double m
     return v;
 }
 
+// Writes the keys of one prepared value into every slot (variant) its
+// feature uses; `low` is ORed into the keys of values that are neither NaN
+// nor in the zero band (the complete-tree kernel keeps only their high bits).
 template <int STRIDE>
-__device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, double v) {
+__device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, double v, int low = 0) {
     const bool nan = v != v;
-    const int k = a.cast_f32 ? key32(__double2float_rn(v)) : key32(__double2float_rd(v));
+    const int k = (a.cast_f32 ? key32(__double2float_rn(v)) : key32(__double2float_rd(v))) | low;
     const bool zero = nan || fabs(v) <= kZeroThr;
     if (s.x >= 0) col[s.x * STRIDE] = nan ? INT_MAX : k;
     if (s.y >= 0) col[s.y * STRIDE] = nan ? INT_MIN : k;

@@ -35,7 +35,6 @@ struct HeapArgs {
     int depth, rows, leaf32, buffers;
     int slot_bits;               // low bits of a split word holding the slot
     const unsigned char* trees;  // whole chunks of heap_record_bytes(depth, leaf32) records, inert trees last
-    const int* tfull;            // [padded trees * (2^depth - 1)]: full threshold key of each split
     const int* node_ids;         // [T * (2^depth - 1)]: file node of each heap split, -1 for padding
     int* status;
 };

@@ -9,12 +9,14 @@
 //
 //     word = (T & ~mask) | slot          mask = 2^slot_bits - 1
 //
-// so a step compares the row's key k against the threshold's high bits:
-// k > (word | mask) proves k > T and k < (word & ~mask) proves k <= T. When
-// k and T agree in those high bits (a float32 within a relative 2^-(23 -
-// slot_bits) of the threshold: rare), the split is decided exactly from the
-// full threshold key kept in a global array, and for float64 models on a
-// full-key tie from the doubles, as the generic kernel does.
+// and the row's key table holds k' = k | mask for every finite key, so a
+// step is one signed compare, k' > word: exact whenever k and T differ in
+// their high bits. When they agree (a float32 within a relative 2^-(23 -
+// slot_bits) of the threshold: rare) the walk notes a tie for the tree, and
+// after the chunk's walk the tied trees are walked again with every tied
+// split decided by the reference's own comparison of the prepared double
+// against the file threshold. NaN and zero-band keys (INT32_MAX, INT32_MIN)
+// never tie with a threshold.
 //
 // Work split. A CTA owns R rows for the whole ensemble: their key tables
 // ([slot][R] int32, lane l always reading bank l) stay in shared memory. Four
@@ -163,7 +165,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
 // values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
 template <int STRIDE, typename XT>
 __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
-                             double* tile, int lane, int f_begin, int f_end) {
+                             double* tile, int lane, int f_begin, int f_end, int low) {
     constexpr int kPerLoad = 32 / kTile;  // rows covered by one warp-wide load
     const int sub = lane / kTile, f_in = lane % kTile;
     double raw[kTile], next[kTile];
@@ -193,7 +195,7 @@ __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long
         __syncwarp();
         const int nf = min(kTile, f_end - f0);
         for (int j = 0; j < nf; ++j) {
-            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kTile + 1) + j]);
+            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kTile + 1) + j], low);
         }
         __syncwarp();
 #pragma unroll
@@ -201,62 +203,70 @@ __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long
     }
 }
 
-// The exact decision of a split whose packed word tied with the row's key:
-// the full threshold key, then (float64 models, equal keys) the doubles.
-template <bool TIES, typename XT>
-__device__ __noinline__ bool tied_right(const ForestArgs& a, const HeapArgs& h, const XT* __restrict__ x, long long row,
-                                        long long batch, int key, int tree, int split, bool live) {
-    const int splits = (1 << h.depth) - 1;
-    const int t = __ldg(h.tfull + static_cast<size_t>(tree) * splits + split);
-    if (TIES && live && key == t) {
-        return exact_right(a, x, row, batch, __ldg(h.node_ids + static_cast<size_t>(tree) * splits + split));
+// One tree walked exactly for one row: the packed compare where the high
+// bits differ, the reference's comparison of the prepared double with the
+// file threshold (exact_right) where they tie. Returns the heap index of the
+// leaf reached. Only trees whose fast walk met a tie come here.
+template <int D, int R, typename XT>
+__device__ __forceinline__ uint32_t walk_exact(const ForestArgs& a, const HeapArgs& h, uint32_t base, uint32_t col,
+                                            uint32_t mask, int tree, const XT* __restrict__ x, long long row,
+                                            long long batch) {
+    constexpr int kSplits = (1 << D) - 1;
+    uint32_t i = 0;
+    for (int d = 0; d < D; ++d) {
+        const uint32_t n = lds_u32(base + 4 * i);
+        const int k = lds_s32(col + (n & mask) * (R * 4));
+        bool right = k > static_cast<int>(n);
+        if (static_cast<uint32_t>(k ^ static_cast<int>(n)) <= mask && tree < a.T) {
+            const int node = __ldg(h.node_ids + static_cast<size_t>(tree) * kSplits + i);
+            if (node >= 0) right = exact_right(a, x, row, batch, node);
+        }
+        i = 2 * i + (right ? 2u : 1u);
     }
-    return key > t;
+    return i;
 }
 
 // Walks the kTrees trees of the chunk at shared address `buf` for one row and
 // adds the leaves of the first `live` of them, in order, to `part`.
-template <int D, int R, bool LEAF32, bool TIES, typename XT>
+template <int D, int R, bool LEAF32, typename XT>
 __device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
                                            uint32_t mask, int chunk, int live, const XT* x, long long row,
                                            long long batch, double& part) {
     constexpr int kSplits = (1 << D) - 1;
     constexpr int kRec = record_bytes(D, LEAF32);
     constexpr int kLeafBytes = LEAF32 ? 4 : 8;
-    constexpr int kShift = R == 128 ? 9 : (R == 64 ? 8 : 7);  // log2(R * 4): bytes of one slot's column
-    static_assert(R == 128 || R == 64 || R == 32, "rows per CTA");
-    uint32_t p[kTrees];
+    uint32_t p[kTrees], go_left[kTrees];
+    bool tie[kTrees];
 #pragma unroll
-    for (int t = 0; t < kTrees; ++t) p[t] = buf + t * kRec;
+    for (int t = 0; t < kTrees; ++t) {
+        p[t] = buf + t * kRec;
+        go_left[t] = 4u - p[t];  // left child of the split at byte address q: 2q + go_left
+        tie[t] = false;
+    }
 #pragma unroll
     for (int d = 0; d < D; ++d) {
         uint32_t n[kTrees];
         int k[kTrees];
-        bool right[kTrees];
 #pragma unroll
         for (int t = 0; t < kTrees; ++t) n[t] = lds_u32(p[t]);
 #pragma unroll
-        for (int t = 0; t < kTrees; ++t) k[t] = lds_s32(col + ((n[t] & mask) << kShift));
-        bool tie = false;
+        for (int t = 0; t < kTrees; ++t) k[t] = lds_s32(col + (n[t] & mask) * (R * 4));
 #pragma unroll
         for (int t = 0; t < kTrees; ++t) {
-            right[t] = k[t] > static_cast<int>(n[t] | mask);
-            tie |= static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask;
+            tie[t] |= static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask;
+            p[t] = 2 * p[t] + go_left[t] + (k[t] > static_cast<int>(n[t]) ? 4u : 0u);
         }
-        if (__any_sync(0xffffffffu, tie)) {
+    }
+    bool any = false;
 #pragma unroll
-            for (int t = 0; t < kTrees; ++t) {
-                if (static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask) {
-                    const uint32_t base = buf + t * kRec;
-                    right[t] = tied_right<TIES>(a, h, x, row, batch, k[t], chunk * kTrees + t,
-                                                static_cast<int>((p[t] - base) >> 2), t < live);
-                }
+    for (int t = 0; t < kTrees; ++t) any |= tie[t];
+    if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+        for (int t = 0; t < kTrees; ++t) {
+            if (tie[t]) {
+                const uint32_t base = buf + t * kRec;
+                p[t] = base + 4 * walk_exact<D, R>(a, h, base, col, mask, chunk * kTrees + t, x, row, batch);
             }
-        }
-#pragma unroll
-        for (int t = 0; t < kTrees; ++t) {
-            const uint32_t base = buf + t * kRec;
-            p[t] = 2 * p[t] - base + (right[t] ? 8u : 4u);
         }
     }
 #pragma unroll
@@ -269,8 +279,8 @@ __device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& 
     }
 }
 
-template <int D, int R, bool LEAF32, bool TIES, typename XT>
-__global__ void __launch_bounds__(kTeams * R) heap_kernel(const ForestArgs a, const HeapArgs h,
+template <int D, int R, bool LEAF32, typename XT>
+__global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a, const HeapArgs h,
                                                           const XT* __restrict__ x, long long batch,
                                                           double* __restrict__ out) {
     constexpr int kChunkBytes = kTrees * record_bytes(D, LEAF32);
@@ -335,7 +345,8 @@ __global__ void __launch_bounds__(kTeams * R) heap_kernel(const ForestArgs a, co
             const int per = (a.F + kTeams - 1) / kTeams;
             const int f_begin = min(a.F, team * per), f_end = min(a.F, f_begin + per);
             double* tile = reinterpret_cast<double*>(smem + L.ring1 + warp * kTileBytes);
-            prepare_rows<R>(a, x, row0 + slice * 32, batch, keys + slice * 32, tile, lane, f_begin, f_end);
+            prepare_rows<R>(a, x, row0 + slice * 32, batch, keys + slice * 32, tile, lane, f_begin, f_end,
+                            static_cast<int>(mask));
             if (team == 0) keys[a.pad_slot * R + slice * 32 + lane] = INT_MIN;
         }
         __syncthreads();
@@ -360,7 +371,7 @@ __global__ void __launch_bounds__(kTeams * R) heap_kernel(const ForestArgs a, co
                     const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u));
                     ++consumed[b];
                     if (ok) {
-                        walk_chunk<D, R, LEAF32, TIES>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
+                        walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
                                                        min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
                     }
                     // Every thread of the team is done with buffer b.
@@ -414,41 +425,37 @@ __global__ void __launch_bounds__(kTeams * R) heap_kernel(const ForestArgs a, co
     }
 }
 
-template <int D, int R, bool LEAF32, bool TIES, typename XT>
+template <int D, int R, bool LEAF32, typename XT>
 void* heap_of() {
-    return reinterpret_cast<void*>(&heap_kernel<D, R, LEAF32, TIES, XT>);
+    return reinterpret_cast<void*>(&heap_kernel<D, R, LEAF32, XT>);
 }
 
 template <int D, int R>
-void* pick_leaf(bool leaf32, bool ties, bool f64) {
-    if (leaf32) {
-        if (ties) return f64 ? heap_of<D, R, true, true, double>() : heap_of<D, R, true, true, float>();
-        return f64 ? heap_of<D, R, true, false, double>() : heap_of<D, R, true, false, float>();
-    }
-    if (ties) return f64 ? heap_of<D, R, false, true, double>() : heap_of<D, R, false, true, float>();
-    return f64 ? heap_of<D, R, false, false, double>() : heap_of<D, R, false, false, float>();
+void* pick_leaf(bool leaf32, bool f64) {
+    if (leaf32) return f64 ? heap_of<D, R, true, double>() : heap_of<D, R, true, float>();
+    return f64 ? heap_of<D, R, false, double>() : heap_of<D, R, false, float>();
 }
 
 template <int D>
-void* pick_rows(int rows, bool leaf32, bool ties, bool f64) {
+void* pick_rows(int rows, bool leaf32, bool f64) {
     switch (rows) {
-        case 128: return pick_leaf<D, 128>(leaf32, ties, f64);
-        case 64: return pick_leaf<D, 64>(leaf32, ties, f64);
-        case 32: return pick_leaf<D, 32>(leaf32, ties, f64);
+        case 128: return pick_leaf<D, 128>(leaf32, f64);
+        case 64: return pick_leaf<D, 64>(leaf32, f64);
+        case 32: return pick_leaf<D, 32>(leaf32, f64);
     }
     return nullptr;
 }
 
-void* pick_heap(int depth, int rows, bool leaf32, bool ties, bool f64) {
+void* pick_heap(int depth, int rows, bool leaf32, bool f64) {
     switch (depth) {
-        case 1: return pick_rows<1>(rows, leaf32, ties, f64);
-        case 2: return pick_rows<2>(rows, leaf32, ties, f64);
-        case 3: return pick_rows<3>(rows, leaf32, ties, f64);
-        case 4: return pick_rows<4>(rows, leaf32, ties, f64);
-        case 5: return pick_rows<5>(rows, leaf32, ties, f64);
-        case 6: return pick_rows<6>(rows, leaf32, ties, f64);
-        case 7: return pick_rows<7>(rows, leaf32, ties, f64);
-        case 8: return pick_rows<8>(rows, leaf32, ties, f64);
+        case 1: return pick_rows<1>(rows, leaf32, f64);
+        case 2: return pick_rows<2>(rows, leaf32, f64);
+        case 3: return pick_rows<3>(rows, leaf32, f64);
+        case 4: return pick_rows<4>(rows, leaf32, f64);
+        case 5: return pick_rows<5>(rows, leaf32, f64);
+        case 6: return pick_rows<6>(rows, leaf32, f64);
+        case 7: return pick_rows<7>(rows, leaf32, f64);
+        case 8: return pick_rows<8>(rows, leaf32, f64);
     }
     return nullptr;
 }
@@ -484,7 +491,7 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
                  std::string& err) {
     const HeapArgs& h = f.heap;
     const bool f64 = dtype == 2;
-    void* k = pick_heap(h.depth, h.rows, h.leaf32, !f.args.cast_f32, f64);
+    void* k = pick_heap(h.depth, h.rows, h.leaf32, f64);
     if (!k) {
         err = "no complete-tree kernel for this model";
         return false;

@@ -441,7 +441,6 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         const size_t chunk = static_cast<size_t>(heap_chunk_trees());
         const size_t padded = (T + chunk - 1) / chunk * chunk;
         std::vector<unsigned char> host(padded * rec, 0);
-        std::vector<int32_t> full(padded * splits, INT32_MAX);
         for (size_t t = 0; t < padded; ++t) {
             uint32_t* w = reinterpret_cast<uint32_t*>(host.data() + t * rec);
             const int32_t* src = t < T ? v->heap_words + t * splits * 2 : nullptr;
@@ -449,7 +448,6 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
                 const int32_t thr = src ? src[2 * i] : INT32_MAX;
                 const int32_t slot = src ? src[2 * i + 1] : v->pad_slot;
                 w[i] = (static_cast<uint32_t>(thr) & ~mask) | static_cast<uint32_t>(slot);
-                full[t * splits + i] = thr;
             }
         }
         for (size_t t = 0; t < T; ++t) {
@@ -466,15 +464,11 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         }
         void* trees = nullptr;
         void* ids = nullptr;
-        void* tfull = nullptr;
         if (!device_alloc(&trees, host.size(), e) ||
             !ok(cudaMemcpy(trees, host.data(), host.size(), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
-            !device_alloc(&tfull, full.size() * 4, e) ||
-            !ok(cudaMemcpy(tfull, full.data(), full.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
             !device_alloc(&ids, T * splits * 4, e) ||
             !ok(cudaMemcpy(ids, v->heap_node_id, T * splits * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
             if (trees) cudaFree(trees);
-            if (tfull) cudaFree(tfull);
             if (ids) cudaFree(ids);
             cudaFreeHost(status);
             cudaFree(block);
@@ -482,7 +476,6 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
             return kInternal;
         }
         f.blocks[f.nblocks++] = trees;
-        f.blocks[f.nblocks++] = tfull;
         f.blocks[f.nblocks++] = ids;
         f.heap.depth = D;
         f.heap.rows = rows;
@@ -490,7 +483,6 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         f.heap.leaf32 = f32;
         f.heap.slot_bits = slot_bits;
         f.heap.trees = static_cast<const unsigned char*>(trees);
-        f.heap.tfull = static_cast<const int*>(tfull);
         f.heap.node_ids = static_cast<const int*>(ids);
     }
     if (!prepare_kernels(f, e)) {
