@@ -32,12 +32,14 @@
 // Streaming. Each team streams its trees through a private pair of chunk
 // buffers (4 trees each, one thread walking the 4 side by side), filled by
 // one-dimensional bulk async copies (cp.async.bulk) whose completion counts on
-// one mbarrier per buffer; a team barrier (named barrier j + 1) releases a
-// buffer and the team's first thread refills it two chunks ahead. The device
-// tree array is padded with inert trees to whole chunks, so every copy is a
-// full chunk. Waits are bounded: on timeout the kernel records an error in the
-// forest's status word, waits (bounded) for its own copies in flight, and
-// every thread of the CTA leaves together.
+// one mbarrier per buffer. No warp waits for its teammates: a warp done with
+// a buffer bumps the buffer's counter in shared memory, and the warp whose
+// bump completes the team's count refills the buffer two chunks ahead. The
+// device tree array is padded with inert trees to whole chunks, so every copy
+// is a full chunk. Waits are bounded: a warp whose wait runs out raises the
+// CTA's abort flag, every wait gives up once the flag is up, the CTA leaves
+// at the next round barrier after waiting (bounded) for its copies in flight,
+// and the forest's status word records the error for the host.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -65,7 +67,9 @@ __host__ __device__ constexpr int record_bytes(int depth, bool leaf32) {
 
 __host__ __device__ constexpr int align128(int n) { return (n + 127) & ~127; }
 
-// Shared memory layout (byte offsets): mbarriers [team][2] at 0 | keys
+// Shared memory layout (byte offsets): header (mbarriers [team][2] at 0,
+// buffer-done counters [team][2] at 64, fills issued [team][2] at 96, abort
+// flag at 128) | keys
 // [slots][R] int32 | block partials [2][team][R] double | first buffers of
 // the four teams | second buffers of the four teams. During the prepare the
 // second buffers (not yet refilled) hold the warps' transpose tiles.
@@ -75,7 +79,7 @@ struct Layout {
 
 __host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, int rows) {
     Layout l{};
-    l.keys = 128;
+    l.keys = 256;
     l.parts = l.keys + align128(slots * rows * 4);
     l.ring0 = l.parts + align128(2 * kTeams * rows * 8);
     const int chunk = kTrees * record_bytes(depth, leaf32);
@@ -102,8 +106,9 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
-// Waits for phase `parity` of `bar` to complete; false after kSpinLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for phase `parity` of `bar` to complete; false after kSpinLimit polls
+// or as soon as `*abort` (when given) is raised.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr) {
     for (long long i = 0; i < kSpinLimit; ++i) {
         uint32_t done;
         asm volatile(
@@ -112,19 +117,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "r"(smem_u32(bar)), "r"(parity)
             : "memory");
         if (done) return true;
+        if (abort && *abort) return false;
     }
     return false;
-}
-
-// Named barrier `id` over `threads` threads that also ORs `v` across them.
-__device__ __forceinline__ bool team_sync_or(int id, int threads, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, %2, %3, p; selp.u32 %0, 1, 0, q; }"
-        : "=r"(r)
-        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
-        : "memory");
-    return r != 0;
 }
 
 __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
@@ -160,15 +155,14 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
 
 // Keys of the 32 rows row0 .. row0 + 31 for features [f_begin, f_end): the
 // warp reads kTile features of all 32 rows per step (four coalesced loads of
-// 8 rows x kTile values, the next step's loads in flight meanwhile), stages
-// them in `tile` ([32][kTile + 1] doubles) and each lane turns its own row's
-// values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
+// 8 rows x kTile values; the next two steps' loads are in flight meanwhile),
+// stages them in `tile` ([32][kTile + 1] doubles) and each lane turns its own
+// row's values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
 template <int STRIDE, typename XT>
 __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
                              double* tile, int lane, int f_begin, int f_end, int low) {
     constexpr int kPerLoad = 32 / kTile;  // rows covered by one warp-wide load
     const int sub = lane / kTile, f_in = lane % kTile;
-    double raw[kTile], next[kTile];
     auto load = [&](int f0, double (&v)[kTile]) {
         const int feat = f0 + f_in;
 #pragma unroll
@@ -177,9 +171,7 @@ __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long
             v[i] = (feat < f_end && row < batch) ? load_x(x + row * a.F + feat) : 0.0;
         }
     };
-    if (f_begin < f_end) load(f_begin, raw);
-    for (int f0 = f_begin; f0 < f_end; f0 += kTile) {
-        if (f0 + kTile < f_end) load(f0 + kTile, next);
+    auto stage = [&](int f0, const double (&v)[kTile]) {
         const int feat = f0 + f_in;
         double mean = 0.0, scale = 1.0;
         if (a.standardize && feat < f_end) {
@@ -190,16 +182,29 @@ __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long
         for (int i = 0; i < kTile; ++i) {
             const long long row = row0 + i * kPerLoad + sub;
             tile[(i * kPerLoad + sub) * (kTile + 1) + f_in] =
-                (feat < f_end && row < batch) ? finish(a, raw[i], mean, scale) : 0.0;
+                (feat < f_end && row < batch) ? finish(a, v[i], mean, scale) : 0.0;
         }
+    };
+    auto keys_of = [&](int f0) {
         __syncwarp();
         const int nf = min(kTile, f_end - f0);
         for (int j = 0; j < nf; ++j) {
             put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kTile + 1) + j], low);
         }
         __syncwarp();
-#pragma unroll
-        for (int i = 0; i < kTile; ++i) raw[i] = next[i];
+    };
+    double even[kTile], odd[kTile];
+    load(f_begin, even);
+    load(f_begin + kTile, odd);
+    for (int f0 = f_begin; f0 < f_end; f0 += 2 * kTile) {
+        stage(f0, even);
+        load(f0 + 2 * kTile, even);
+        keys_of(f0);
+        if (f0 + kTile < f_end) {
+            stage(f0 + kTile, odd);
+            load(f0 + 3 * kTile, odd);
+            keys_of(f0 + kTile);
+        }
     }
 }
 
@@ -287,14 +292,17 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     constexpr int kWarpsPerTeam = R / 32;
     extern __shared__ __align__(128) unsigned char smem[];
     const Layout L = layout_of(a.slots, D, LEAF32, R);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [team][buffer]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                // [team][buffer]
+    unsigned* done = reinterpret_cast<unsigned*>(smem + 64);         // [team][buffer]: warps done, cumulative
+    unsigned* fills = reinterpret_cast<unsigned*>(smem + 96);        // [team][buffer]: copies issued
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + 128);
     int* keys = reinterpret_cast<int*>(smem + L.keys);
     double* parts = reinterpret_cast<double*>(smem + L.parts);
 
     const int tid = threadIdx.x;
     const int team = tid / R, r = tid % R;
     const int warp = tid >> 5, lane = tid & 31;
-    const bool producer = r == 0;  // issues the team's copies
+    const bool producer = r == 0;  // issues the team's first two copies of a row group
     const int chunks = (a.T + kTrees - 1) / kTrees;
     const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
     const int rounds = (blocks + kTeams - 1) / kTeams;
@@ -313,7 +321,12 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     uint64_t* team_bar = bar + 2 * team;
 
     if (tid == 0) {
-        for (int b = 0; b < 2 * kTeams; ++b) mbar_init(&bar[b]);
+        for (int b = 0; b < 2 * kTeams; ++b) {
+            mbar_init(&bar[b]);
+            done[b] = 0u;
+            fills[b] = 0u;
+        }
+        *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (blockIdx.x < groups) {
             const long long r0 = static_cast<long long>(blockIdx.x) * R;
@@ -323,14 +336,14 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     __syncthreads();
 
     // Buffer b's k-th fill completes its barrier's phase k: every thread of
-    // the team counts the fills it has consumed, the producer those it issued
+    // the team counts the fills it has consumed; `fills` counts those issued
     // (to wait out copies in flight before an early exit).
-    uint32_t consumed[2] = {0u, 0u}, issued[2] = {0u, 0u};
+    uint32_t consumed[2] = {0u, 0u};
     auto issue = [&](int q) {
         const int b = q & 1;
         bulk_load(b ? buf1 : buf0, h.trees + static_cast<size_t>(chunk_at(q)) * kChunkBytes, kChunkBytes,
                   &team_bar[b]);
-        ++issued[b];
+        atomicAdd(&fills[2 * team + b], 1u);
     };
     if (producer && n_team > 0 && blockIdx.x < groups) issue(0);
 
@@ -357,33 +370,40 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
         }
 
         double acc = 0.0;  // team 0: the row's sum over the rounds done
-        bool bad = false;  // a wait of this team timed out (team-uniform)
+        bool bad = false;  // the CTA is aborting (uniform after each round barrier)
         int q = 0;         // position in the team's chunk list
         for (int k = 0; k < rounds; ++k) {
             const int block = team + kTeams * k;
-            if (block < blocks && !bad) {
+            if (block < blocks) {
                 const int c0 = block * kChunksPerBlock;
                 const int cn = min(kChunksPerBlock, chunks - c0);
                 double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
                 for (int c = 0; c < cn; ++c, ++q) {
                     const int b = q & 1;
                     // Warp-uniform: the walk's votes need every lane.
-                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u));
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, abort));
                     ++consumed[b];
                     if (ok) {
                         walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
-                                                       min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
+                                                 min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
+                    } else if (lane == 0) {
+                        *abort = 1;
                     }
-                    // Every thread of the team is done with buffer b.
-                    if (team_sync_or(team + 1, R, !ok)) {
-                        bad = true;
-                        break;
+                    __syncwarp();
+                    if (lane == 0) {
+                        // This warp's reads of buffer b are done; the team's
+                        // last warp to get here refills it.
+                        __threadfence_block();
+                        const unsigned before = atomicAdd(&done[2 * team + b], 1u);
+                        if (before % kWarpsPerTeam == kWarpsPerTeam - 1 && q + 2 < n_team && !*abort) {
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            issue(q + 2);
+                        }
                     }
-                    if (producer && q + 2 < n_team) issue(q + 2);
                 }
                 parts[((k & 1) * kTeams + team) * R + r] = part;
             }
-            if (__syncthreads_or(bad)) {
+            if (__syncthreads_or(*abort)) {
                 bad = true;
                 break;
             }
@@ -404,7 +424,8 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
             if (producer) {
                 if (team == 0) atomicExch(h.status, 1);
                 for (int b = 0; b < 2; ++b) {
-                    if (issued[b] > 0) mbar_wait(&team_bar[b], (issued[b] - 1u) & 1u);
+                    const unsigned n = fills[2 * team + b];
+                    if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u);
                 }
             }
             return;

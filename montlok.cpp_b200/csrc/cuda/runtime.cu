@@ -434,12 +434,17 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         const bool f32 = v->heap_leaf_f32 != 0;
         const size_t splits = (size_t{1} << D) - 1, leaves = size_t{1} << D;
         const size_t rec = static_cast<size_t>(heap_record_bytes(D, f32));
-        const int slot_bits = heap_slot_bits(v->slots);
-        const uint32_t mask = (1u << slot_bits) - 1u;
         // Whole chunks: the tail is inert trees (every split goes left, to
         // leaves of 0.0), which the kernel walks but never adds.
         const size_t chunk = static_cast<size_t>(heap_chunk_trees());
         const size_t padded = (T + chunk - 1) / chunk * chunk;
+        // The split word keeps as few low bits for the slot as the slots the
+        // words name need (the pad slot only when padding splits or inert
+        // trees exist): every bit left to the threshold halves the ties.
+        int32_t top_slot = padded > T ? v->pad_slot : 0;
+        for (size_t i = 0; i < T * splits; ++i) top_slot = std::max(top_slot, v->heap_words[2 * i + 1]);
+        const int slot_bits = heap_slot_bits(top_slot + 1);
+        const uint32_t mask = (1u << slot_bits) - 1u;
         std::vector<unsigned char> host(padded * rec, 0);
         for (size_t t = 0; t < padded; ++t) {
             uint32_t* w = reinterpret_cast<uint32_t*>(host.data() + t * rec);
