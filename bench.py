@@ -21,6 +21,13 @@ line:
 
 ``--impl reference`` times the reference's CPU implementation alone, with all
 host threads, on the same workload and prints the same line.
+
+``--config c5`` is the latency configuration: calls of 1, 8 and 64 rows
+back to back through montlok_model_predict (host buffers; the library
+replays a cached CUDA graph per call shape), timed per call inside the
+library; the line reports p50/p99 microseconds per call size, the value being
+the p50 of the 64-row calls, with the reference's own per-call latency on the
+host cores beside it.
 """
 
 from __future__ import annotations
@@ -167,6 +174,105 @@ def run_reference(args, cfg, model: bytes, x: np.ndarray) -> dict:
             "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+LATENCY_SIZES = (1, 8, 64)
+
+
+def latency_stats(samples_ns: np.ndarray) -> dict:
+    return {"p50_us": float(np.percentile(samples_ns, 50)) / 1e3, "p99_us": float(np.percentile(samples_ns, 99)) / 1e3,
+            "mean_us": float(np.mean(samples_ns)) / 1e3, "calls": int(len(samples_ns))}
+
+
+def latency_line(args, cfg, stats: dict, impl: str | None) -> dict:
+    p50 = stats["64"]["p50_us"]
+    line = {"metric": f"p50 us per 64-row call ({cfg.name}: {cfg.describe})", "value": p50, "unit": "us",
+            "n_gpus": args.gpus, "steps": args.calls, "warmup": args.warmup, "ms_per_step": p50 / 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: {cfg.describe}", "call_rows": list(LATENCY_SIZES),
+                       "timing": "per call, inside the library, host buffers in and out"},
+            "latency": stats}
+    if impl:
+        line["impl"] = impl
+    return line
+
+
+def reference_latency(args, model: bytes, x: np.ndarray, threads: int) -> tuple[dict, str]:
+    """Per-call latency of the reference runtime (or None without it)."""
+    import oracle
+
+    if not oracle.available_reference():
+        return {}, "unavailable"
+    ref = oracle.Reference()
+    ref.set_threads(threads)
+    h = ref.open(model)
+    stats = {}
+    try:
+        for n in LATENCY_SIZES:
+            rows = x[: len(x) // n * n].reshape(-1, n * x.shape[1])
+            calls = max(50, min(args.calls, int(args.cpu_seconds / len(LATENCY_SIZES) * 1e6 / (40.0 * n))))
+            stats[str(n)] = latency_stats(ref.time_calls(h, rows, n, calls, max(10, calls // 10)))
+    finally:
+        ref.close(h)
+    return stats, "reference"
+
+
+def run_latency(args, cfg) -> None:
+    """The small-batch configuration on rank 0's GPU (other ranks idle)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    model_bytes = cfg.model().to_bytes()
+    x = cfg.inputs(batch=64 * 256)
+    threads = os.cpu_count() or 1
+    if args.impl == "reference":
+        stats, kind = reference_latency(args, model_bytes, x, threads)
+        if not stats:
+            print(json.dumps({"impl": "reference", "unavailable": "reference library not built"}), flush=True)
+            return
+        line = latency_line(args, cfg, stats, "reference")
+        line["cpu_baseline"] = {"value": stats["64"]["p50_us"], "unit": "us", "cores": threads, "kind": kind,
+                                "sample": "per-call latency, calls of 1, 8 and 64 rows"}
+        line["e2e"] = {"value": stats["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        print(json.dumps(line), flush=True)
+        return
+    import torch
+
+    import montlok
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    model = montlok.load(model_bytes)
+    clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    stats = {}
+    for n in LATENCY_SIZES:
+        rows = x[: len(x) // n * n].reshape(-1, n * model.features)
+        samples, _ = montlok._core.bench(model, rows, batch=n, iterations=args.calls)
+        stats[str(n)] = latency_stats(samples)
+    # Device time of one 64-row predict (inputs resident), CUDA events.
+    xd = torch.from_numpy(np.ascontiguousarray(x[:64])).cuda()
+    od = torch.empty((64, model.outputs), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.Stream()
+    for _ in range(args.warmup):
+        model.predict_device(xd.data_ptr(), 64, od.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(100):
+        model.predict_device(xd.data_ptr(), 64, od.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    line = latency_line(args, cfg, stats, None)
+    line["device_us_per_64_rows"] = start.elapsed_time(end) * 10.0
+    line["e2e"] = {"value": stats["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 64 * model.features * 8,
+                   "d2h_bytes_per_step": 64 * model.outputs * 8}
+    line["roofline"] = None
+    line["gpu_launches"] = args.calls * len(LATENCY_SIZES)
+    line["clocks"] = clocks.stop()
+    if not args.no_cpu:
+        ref_stats, kind = reference_latency(args, model_bytes, x, threads)
+        if ref_stats:
+            line["cpu_baseline"] = {"value": ref_stats["64"]["p50_us"], "unit": "us", "cores": threads, "kind": kind,
+                                    "sample": "per-call latency, calls of 1, 8 and 64 rows", "latency": ref_stats}
+    print(json.dumps(line), flush=True)
+
+
 def workload(cfg, args) -> dict:
     return {"workload": f"{cfg.name}: {cfg.describe}", "rows_per_rank": args.rows or cfg.batch,
             "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"rows sharded, {args.gpus} GPU(s)"}
@@ -184,12 +290,16 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=8.0)
     parser.add_argument("--reference-rows", type=int, default=65536)
     parser.add_argument("--no-cpu", action="store_true")
+    parser.add_argument("--calls", type=int, default=20000, help="timed calls per size (latency configuration)")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
 
     from montlok import synth
 
     cfg = synth.CONFIGS[args.config]
+    if args.config == "c5":
+        run_latency(args, cfg)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

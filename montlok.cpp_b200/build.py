@@ -58,7 +58,8 @@ def build(clean: bool = False, verbose: bool = False) -> Path:
     if clean and OUT.exists():
         shutil.rmtree(OUT)
     OUT.mkdir(parents=True, exist_ok=True)
-    headers = sorted(CSRC.rglob("*.h*")) + sorted((REPO / "include").rglob("*.h"))
+    headers = sorted(p for pattern in ("*.h", "*.hpp", "*.cuh") for p in CSRC.rglob(pattern)) + sorted(
+        (REPO / "include").rglob("*.h"))
     objects = []
     for src in sorted((CSRC / "core").glob("*.cpp")):
         obj = OUT / (src.stem + ".o")

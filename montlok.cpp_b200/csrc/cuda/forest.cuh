@@ -40,6 +40,7 @@ struct HeapArgs {
 };
 
 struct DevForest {
+    unsigned long long uid = 0;  // distinct for every forest uploaded by this process
     int device = 0;
     int sm_count = 0;
     ForestArgs args{};
@@ -50,15 +51,16 @@ struct DevForest {
 };
 
 // Queues one predict (out != nullptr) or leaf-index (leaves != nullptr) pass
-// over device buffers on `stream`. `scratch` holds scratch_bytes(f) bytes of
+// over device buffers on `stream`. `scratch` holds scratch_bytes(f, batch) bytes of
 // device memory (nullptr when that is 0). Returns false with `err` set.
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
                    cudaStream_t stream, std::string& err, int* scratch);
 
-// Device scratch a launch needs: 0 unless the key table of a warp exceeds
-// shared memory (models with thousands of features), when the tables live in
-// global memory, one per resident warp.
-size_t scratch_bytes(const DevForest& f);
+// Device scratch a launch of `batch` rows needs: key tables in global memory
+// when a warp's table exceeds shared memory (models with thousands of
+// features), one per resident warp; then, for batches the small-batch
+// complete-tree kernel takes, its per-tree leaf values and block sums.
+size_t scratch_bytes(const DevForest& f, long long batch);
 
 // One-time per-device kernel attributes (dynamic shared memory limits).
 bool prepare_kernels(const DevForest& f, std::string& err);
@@ -69,6 +71,14 @@ bool heap_plan(int slots, int depth, bool leaf32, int& rows, int& buffers);
 int heap_record_bytes(int depth, bool leaf32);
 int heap_chunk_trees();
 int heap_slot_bits(int slots);
+
+// Tree-parallel complete-tree kernel for small batches: device scratch it
+// needs, whether it takes `batch` rows, launch (`scratch` holds
+// latency_scratch_bytes(f) bytes).
+size_t latency_scratch_bytes(const DevForest& f);
+bool latency_fits(const DevForest& f, long long batch);
+bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
+                    std::string& err, void* scratch);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
 

@@ -235,16 +235,29 @@ bool prepare_kernels(const DevForest& f, std::string& err) {
     return true;
 }
 
-size_t scratch_bytes(const DevForest& f) {
+// Global key tables of the generic kernel (models whose 32-row key table
+// overflows shared memory), then the small-batch kernel's sums.
+size_t key_scratch_bytes(const DevForest& f) {
     const Shape s = shape_of(f.args);
     if (!s.global_keys) return 0;
-    return static_cast<size_t>(f.sm_count) * 4 * s.warps_per_cta * f.args.slots * 32 * sizeof(int);
+    return (static_cast<size_t>(f.sm_count) * 4 * s.warps_per_cta * f.args.slots * 32 * sizeof(int) + 255) &
+           ~size_t{255};
+}
+
+size_t scratch_bytes(const DevForest& f, long long batch) {
+    return key_scratch_bytes(f) + (latency_fits(f, batch) ? latency_scratch_bytes(f) : 0);
 }
 
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
                    cudaStream_t stream, std::string& err, int* scratch) {
     if (batch <= 0) return true;
-    if (out && !leaves && f.heap.depth > 0) return launch_heap(f, dtype, x, batch, out, stream, err);
+    if (out && !leaves && f.heap.depth > 0) {
+        if (scratch && latency_fits(f, batch)) {
+            return launch_latency(f, dtype, x, batch, out, stream, err,
+                                  reinterpret_cast<unsigned char*>(scratch) + key_scratch_bytes(f));
+        }
+        return launch_heap(f, dtype, x, batch, out, stream, err);
+    }
     const ForestArgs& a = f.args;
     const Shape s = shape_of(a);
     const bool ties = !a.cast_f32;

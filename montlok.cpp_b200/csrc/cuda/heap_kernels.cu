@@ -231,12 +231,12 @@ __device__ __forceinline__ uint32_t walk_exact(const ForestArgs& a, const HeapAr
     return i;
 }
 
-// Walks the kTrees trees of the chunk at shared address `buf` for one row and
-// adds the leaves of the first `live` of them, in order, to `part`.
+// Walks the kTrees trees of the chunk at shared address `buf` (file trees
+// tree0 .. tree0 + kTrees - 1) for one row; v[t] receives tree t's leaf value.
 template <int D, int R, bool LEAF32, typename XT>
-__device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
-                                           uint32_t mask, int chunk, int live, const XT* x, long long row,
-                                           long long batch, double& part) {
+__device__ __forceinline__ void walk_leaves(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
+                                            uint32_t mask, int tree0, const XT* x, long long row, long long batch,
+                                            double (&v)[kTrees]) {
     constexpr int kSplits = (1 << D) - 1;
     constexpr int kRec = record_bytes(D, LEAF32);
     constexpr int kLeafBytes = LEAF32 ? 4 : 8;
@@ -270,17 +270,28 @@ __device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& 
         for (int t = 0; t < kTrees; ++t) {
             if (tie[t]) {
                 const uint32_t base = buf + t * kRec;
-                p[t] = base + 4 * walk_exact<D, R>(a, h, base, col, mask, chunk * kTrees + t, x, row, batch);
+                p[t] = base + 4 * walk_exact<D, R>(a, h, base, col, mask, tree0 + t, x, row, batch);
             }
         }
     }
 #pragma unroll
     for (int t = 0; t < kTrees; ++t) {
-        if (t < live) {
-            const uint32_t base = buf + t * kRec;
-            const uint32_t leaf = ((p[t] - base) >> 2) - kSplits;
-            part = __dadd_rn(part, lds_leaf(base + (4u << D) + leaf * kLeafBytes, LEAF32));
-        }
+        const uint32_t base = buf + t * kRec;
+        const uint32_t leaf = ((p[t] - base) >> 2) - kSplits;
+        v[t] = lds_leaf(base + (4u << D) + leaf * kLeafBytes, LEAF32);
+    }
+}
+
+// Walks a chunk and adds the leaves of its first `live` trees, in order, to `part`.
+template <int D, int R, bool LEAF32, typename XT>
+__device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
+                                           uint32_t mask, int chunk, int live, const XT* x, long long row,
+                                           long long batch, double& part) {
+    double v[kTrees];
+    walk_leaves<D, R, LEAF32>(a, h, buf, col, mask, chunk * kTrees, x, row, batch, v);
+#pragma unroll
+    for (int t = 0; t < kTrees; ++t) {
+        if (t < live) part = __dadd_rn(part, v[t]);
     }
 }
 
@@ -446,6 +457,172 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tree-parallel kernel for small batches (at most kLatencyRows rows), where
+// the row-streaming kernel would give one CTA the whole ensemble. CTA
+// (b, g) takes the 64-tree block b for the 32 rows of group g: it bulk-copies
+// the block's trees into shared memory while its threads build the rows' key
+// tables (each thread a few (row, feature) values, all loads in flight at
+// once, the table stride padded to 33 so these scattered writes spread over
+// the banks), its 16 warps walk 4 trees each (lane = row), and 32 threads
+// add the block's 64 leaf values per row in tree order (block 0 onto the
+// base score) into `bpart` ([block][kLatencyRows]). The last CTA of the row
+// group to finish (a device-scope counter, no waiting) adds the block sums
+// in block order and applies the link: the reference's association
+// (trees.cpp:303-388). `count` ([row groups]) is zeroed on the stream before
+// each launch.
+// ---------------------------------------------------------------------------
+constexpr int kLatencyRows = 64;
+constexpr int kLatencyStride = 33;                  // key table row stride (32 rows + 1)
+constexpr int kLatencyWarps = kTreeBlock / kTrees;  // 16: one per 4 trees of the block
+constexpr int kLatencyThreads = 32 * kLatencyWarps;
+constexpr int kSumBatch = 16;                       // final sum: global loads in flight per thread
+
+__host__ __device__ inline int latency_smem(int slots, int depth, bool leaf32) {
+    return 128 + align128(slots * kLatencyStride * 4) + align128(kTreeBlock * record_bytes(depth, leaf32)) +
+           kTreeBlock * 32 * 8;
+}
+
+template <int D, bool LEAF32, typename XT>
+__global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const ForestArgs a, const HeapArgs h,
+                                                                    const XT* __restrict__ x, long long batch,
+                                                                    double* __restrict__ out, double* bpart,
+                                                                    int* count) {
+    constexpr int kRec = record_bytes(D, LEAF32);
+    constexpr int kPerThread = 8;  // values one thread loads per round of the prepare
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    int* flag = reinterpret_cast<int*>(smem + 64);
+    int* keys = reinterpret_cast<int*>(smem + 128);
+    unsigned char* trees = smem + 128 + align128(a.slots * kLatencyStride * 4);
+    double* leafv = reinterpret_cast<double*>(trees + align128(kTreeBlock * kRec));  // [tree][32 rows]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
+    const int block = blockIdx.x % blocks, group = blockIdx.x / blocks;
+    const long long row0 = 32ll * group;
+    const int t0 = block * kTreeBlock;
+    const int nt = min(kTreeBlock, a.T - t0);
+    // Device records are padded to whole chunks of kTrees trees.
+    const int copied = min(kTreeBlock, (a.T + kTrees - 1) / kTrees * kTrees - t0);
+    const uint32_t mask = (1u << h.slot_bits) - 1u;
+
+    if (tid == 0) {
+        mbar_init(bar);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (tid == 0) {
+        bulk_load(smem_u32(trees), h.trees + static_cast<size_t>(t0) * kRec, static_cast<uint32_t>(copied * kRec), bar);
+    }
+    // Keys of the group's live rows: value i is (row row0 + i / F, feature
+    // i % F). Padding rows keep whatever the table holds: their walks read
+    // only in-bounds shared memory (slots come from the split words) and
+    // their leaves are never added.
+    const int values = static_cast<int>(min(32ll, batch - row0)) * a.F;
+    for (int i0 = tid; i0 < values; i0 += kPerThread * kLatencyThreads) {
+        // Every load of the round first (value, slots, preprocess), then the keys.
+        double v[kPerThread], mean[kPerThread], scale[kPerThread];
+        int4 slot[kPerThread];
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+            const int i = i0 + j * kLatencyThreads;
+            const int f = i % a.F;
+            const long long row = row0 + i / a.F;
+            const bool live = i < values;
+            v[j] = live ? load_x(x + row * a.F + f) : 0.0;
+            slot[j] = live ? __ldg(a.slot_of + f) : make_int4(-1, -1, -1, -1);
+            mean[j] = (live && a.standardize) ? __ldg(a.pre_mean + f) : 0.0;
+            scale[j] = (live && a.standardize) ? __ldg(a.pre_scale + f) : 1.0;
+        }
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+            const int i = i0 + j * kLatencyThreads;
+            if (i < values) {
+                put_keys<kLatencyStride>(a, keys + i / a.F, slot[j], finish(a, v[j], mean[j], scale[j]),
+                                         static_cast<int>(mask));
+            }
+        }
+    }
+    if (tid < 32) keys[a.pad_slot * kLatencyStride + tid] = INT_MIN;
+    __syncthreads();
+    if (!__all_sync(0xffffffffu, mbar_wait(bar, 0u))) {
+        if (lane == 0) atomicExch(h.status, 1);
+        return;  // the row group's sum never completes; the host reads the status word
+    }
+    const long long row = row0 + lane;
+    if (warp * kTrees < copied) {
+        double v[kTrees];
+        walk_leaves<D, kLatencyStride, LEAF32>(a, h, smem_u32(trees) + warp * kTrees * kRec,
+                                               smem_u32(keys) + lane * 4, mask, t0 + warp * kTrees, x, row, batch, v);
+#pragma unroll
+        for (int t = 0; t < kTrees; ++t) leafv[(warp * kTrees + t) * 32 + lane] = v[t];
+    }
+    __syncthreads();
+    if (tid < 32 && row < batch) {
+        double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+        for (int t0 = 0; t0 < nt; t0 += 8) {
+            double v[8];  // the loads together, the adds in order
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = t0 + j < nt ? leafv[(t0 + j) * 32 + tid] : 0.0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (t0 + j < nt) acc = __dadd_rn(acc, v[j]);
+            }
+        }
+        __stcg(bpart + static_cast<size_t>(block) * kLatencyRows + row, acc);
+        __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) *flag = atomicAdd(&count[group], 1) == blocks - 1;
+    __syncthreads();
+    if (!*flag || tid >= 32 || row >= batch) return;
+    // Last CTA of the row group: the block sums in order, then mean and link.
+    double v[1] = {__ldcg(bpart + row)};
+    for (int b0 = 1; b0 < blocks; b0 += kSumBatch) {
+        double p[kSumBatch];
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            p[j] = b0 + j < blocks ? __ldcg(bpart + static_cast<size_t>(b0 + j) * kLatencyRows + row) : 0.0;
+        }
+#pragma unroll
+        for (int j = 0; j < kSumBatch; ++j) {
+            if (b0 + j < blocks) v[0] = __dadd_rn(v[0], p[j]);
+        }
+    }
+    if (a.mean) {
+        const int n = __ldg(a.counts);
+        v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
+    }
+    apply_link<1>(a, v, 1);
+    out[row] = v[0];
+}
+
+template <int D, bool LEAF32, typename XT>
+void* latency_of() {
+    return reinterpret_cast<void*>(&latency_kernel<D, LEAF32, XT>);
+}
+
+template <int D>
+void* pick_latency_leaf(bool leaf32, bool f64) {
+    if (leaf32) return f64 ? latency_of<D, true, double>() : latency_of<D, true, float>();
+    return f64 ? latency_of<D, false, double>() : latency_of<D, false, float>();
+}
+
+void* pick_latency(int depth, bool leaf32, bool f64) {
+    switch (depth) {
+        case 1: return pick_latency_leaf<1>(leaf32, f64);
+        case 2: return pick_latency_leaf<2>(leaf32, f64);
+        case 3: return pick_latency_leaf<3>(leaf32, f64);
+        case 4: return pick_latency_leaf<4>(leaf32, f64);
+        case 5: return pick_latency_leaf<5>(leaf32, f64);
+        case 6: return pick_latency_leaf<6>(leaf32, f64);
+        case 7: return pick_latency_leaf<7>(leaf32, f64);
+        case 8: return pick_latency_leaf<8>(leaf32, f64);
+    }
+    return nullptr;
+}
+
 template <int D, int R, bool LEAF32, typename XT>
 void* heap_of() {
     return reinterpret_cast<void*>(&heap_kernel<D, R, LEAF32, XT>);
@@ -545,4 +722,59 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
     return true;
 }
 
+size_t latency_scratch_bytes(const DevForest& f) {
+    if (f.heap.depth <= 0) return 0;
+    const size_t blocks = static_cast<size_t>((f.args.T + kTreeBlock - 1) / kTreeBlock);
+    return blocks * kLatencyRows * sizeof(double) + 2 * sizeof(int);
+}
+
+// The tree-parallel kernel takes batches of at most kLatencyRows rows when
+// the key tables of 32 rows and a whole 64-tree block fit shared memory.
+bool latency_fits(const DevForest& f, long long batch) {
+    const HeapArgs& h = f.heap;
+    if (h.depth <= 0 || batch > kLatencyRows) return false;
+    return latency_smem(f.args.slots, h.depth, h.leaf32) <= kHeapSmemLimit;
+}
+
+bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
+                    std::string& err, void* scratch) {
+    const HeapArgs& h = f.heap;
+    void* k = pick_latency(h.depth, h.leaf32, dtype == 2);
+    if (!k) {
+        err = "no small-batch complete-tree kernel for this model";
+        return false;
+    }
+    const int smem = latency_smem(f.args.slots, h.depth, h.leaf32);
+    {
+        static std::mutex mu;
+        static std::vector<std::pair<void*, int>> set;
+        std::lock_guard<std::mutex> lock(mu);
+        if (std::find(set.begin(), set.end(), std::make_pair(k, f.device)) == set.end()) {
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeapSmemLimit);
+            if (e != cudaSuccess) {
+                err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+                return false;
+            }
+            set.emplace_back(k, f.device);
+        }
+    }
+    const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
+    const int groups = static_cast<int>((batch + 31) / 32);
+    double* bpart = static_cast<double*>(scratch);
+    int* count = reinterpret_cast<int*>(bpart + static_cast<size_t>(blocks) * kLatencyRows);
+    cudaError_t e = cudaMemsetAsync(count, 0, 2 * sizeof(int), stream);
+    if (e != cudaSuccess) {
+        err = std::string("cudaMemsetAsync: ") + cudaGetErrorString(e);
+        return false;
+    }
+    ForestArgs a = f.args;
+    HeapArgs hh = h;
+    void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out, &bpart, &count};
+    e = cudaLaunchKernel(k, blocks * groups, kLatencyThreads, args, smem, stream);
+    if (e != cudaSuccess) {
+        err = std::string("small-batch kernel launch: ") + cudaGetErrorString(e);
+        return false;
+    }
+    return true;
+}
 }  // namespace mlk::cuda

@@ -21,6 +21,7 @@
 #include <memory>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "forest.cuh"
@@ -153,11 +154,28 @@ struct PinnedBuffer {
     }
 };
 
+// A small host-buffer predict captured as a CUDA graph (input copy, kernel,
+// output copy) for one forest, input type and row count, over the buffers
+// it was captured with.
+struct CachedGraph {
+    unsigned long long forest = 0;
+    int dtype = 0;
+    size_t batch = 0;
+    const void* buffers[5] = {};
+    cudaGraphExec_t exec = nullptr;
+    unsigned long long used = 0;
+};
+
 struct Workspace {
     cudaStream_t stream[2] = {nullptr, nullptr};
     DeviceBuffer dx[2], dout[2], scratch;
     PinnedBuffer hx[2], hout[2];
+    std::vector<CachedGraph> graphs;
+    unsigned long long tick = 0;
     ~Workspace() {
+        for (auto& g : graphs) {
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+        }
         for (auto s : stream) {
             if (s) cudaStreamDestroy(s);
         }
@@ -175,6 +193,99 @@ Workspace* workspace(int device, std::string& err) {
         w = std::move(fresh);
     }
     return w.get();
+}
+
+constexpr size_t kGraphRows = 4096;  // host-buffer predicts of at most this many rows replay a graph
+constexpr size_t kGraphCache = 8;    // graphs kept per workspace
+
+// A predict of at most kGraphRows rows from and to host memory: the input is
+// copied into the workspace's pinned staging buffer, a cached graph of
+// (host -> device copy, kernel) runs on the workspace's first stream, the
+// kernel storing its results into pinned host memory directly, and the
+// result is copied out. The graph is captured on the first call with this
+// forest, input type and row count (or after a staging buffer grew), so
+// later calls of the same shape pay one graph launch instead of separate
+// stream operations and kernel launches.
+int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double* out, char* err, size_t errlen) {
+    std::string e;
+    DeviceGuard guard(f.device);
+    Workspace* w = workspace(f.device, e);
+    if (!w) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    const size_t in_bytes = batch * static_cast<size_t>(f.args.F) * (dtype == 1 ? 4 : 8);
+    const size_t out_bytes = batch * static_cast<size_t>(f.args.K) * sizeof(double);
+    const size_t scratch = scratch_bytes(f, static_cast<long long>(batch));
+    if (!w->dx[0].reserve(in_bytes, e) || !w->hx[0].reserve(in_bytes, e) ||
+        !w->hout[0].reserve(out_bytes, e) || (scratch && !w->scratch.reserve(scratch, e))) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    cudaStream_t st = w->stream[0];
+    const void* buffers[5] = {w->dx[0].p, nullptr, w->hx[0].p, w->hout[0].p, scratch ? w->scratch.p : nullptr};
+    CachedGraph* g = nullptr;
+    for (auto& c : w->graphs) {
+        if (c.forest == f.uid && c.dtype == dtype && c.batch == batch && std::equal(buffers, buffers + 5, c.buffers)) {
+            g = &c;
+        }
+    }
+    if (!g) {
+        bool good = ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture", e);
+        if (good) {
+            good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e);
+            if (good && injected("launch")) {
+                e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
+                good = false;
+            }
+            // The kernel stores the results straight into the pinned staging
+            // buffer (host memory the device addresses directly).
+            good = good && launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
+                                         static_cast<double*>(w->hout[0].p), nullptr, st, e,
+                                         static_cast<int*>(w->scratch.p));
+            cudaGraph_t graph = nullptr;
+            const cudaError_t end = cudaStreamEndCapture(st, &graph);
+            if (good) good = ok(end, "cudaStreamEndCapture", e);
+            cudaGraphExec_t exec = nullptr;
+            if (good) good = ok(cudaGraphInstantiate(&exec, graph, 0), "cudaGraphInstantiate", e);
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+            if (good) {
+                if (w->graphs.size() >= kGraphCache) {
+                    auto oldest = std::min_element(w->graphs.begin(), w->graphs.end(),
+                                                   [](const CachedGraph& a, const CachedGraph& b) { return a.used < b.used; });
+                    cudaGraphExecDestroy(oldest->exec);
+                    w->graphs.erase(oldest);
+                }
+                CachedGraph c;
+                c.forest = f.uid;
+                c.dtype = dtype;
+                c.batch = batch;
+                std::copy(buffers, buffers + 5, c.buffers);
+                c.exec = exec;
+                w->graphs.push_back(c);
+                g = &w->graphs.back();
+            }
+        }
+        if (!good) {
+            put_error(err, errlen, e);
+            return kInternal;
+        }
+    }
+    g->used = ++w->tick;
+    std::memcpy(w->hx[0].p, x, in_bytes);
+    bool good = ok(cudaGraphLaunch(g->exec, st), "cudaGraphLaunch", e) &&
+                ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
+    if (good) std::memcpy(out, w->hout[0].p, out_bytes);
+    if (good && f.status_host && *reinterpret_cast<volatile int*>(f.status_host) != 0) {
+        e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
+        good = false;
+    }
+    if (!good) {
+        put_error(err, errlen, e);
+        return kInternal;
+    }
+    return 0;
 }
 
 // A pending chunk whose results sit in a pinned staging buffer.
@@ -205,8 +316,14 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     mlk_cuda_pointer_kind(out, &ko, &dev);
     const bool pin_x = kx == MLK_PTR_PINNED, pin_out = ko == MLK_PTR_PINNED;
     const bool dev_x = kx == MLK_PTR_DEVICE, dev_out = ko == MLK_PTR_DEVICE;
+    if constexpr (std::is_same_v<Out, double>) {
+        if (!leaves && batch <= kGraphRows && !dev_x && !dev_out) return run_small(f, dtype, x, batch, out, err, errlen);
+    }
 
-    const size_t scratch = scratch_bytes(f);
+    // Chunks are `chunk` rows but the last one, which may take another kernel.
+    const size_t tail = batch % chunk;
+    const size_t scratch = std::max(scratch_bytes(f, static_cast<long long>(chunk)),
+                                    tail ? scratch_bytes(f, static_cast<long long>(tail)) : size_t{0});
     if (scratch && !w->scratch.reserve(scratch, e)) {
         put_error(err, errlen, e);
         return kInternal;
@@ -347,6 +464,8 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     DeviceGuard guard(device);
     auto holder = std::make_unique<mlk_dev_forest>();
     DevForest& f = holder->f;
+    static std::atomic<unsigned long long> next_uid{1};
+    f.uid = next_uid.fetch_add(1);
     f.device = device;
     if (!ok(cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute", e)) {
         put_error(err, errlen, e);
@@ -516,7 +635,7 @@ static int device_call(const mlk_dev_forest* forest, int dtype, const void* x, s
     if (batch == 0) return 0;
     std::string e;
     DeviceGuard guard(forest->f.device);
-    const size_t scratch = scratch_bytes(forest->f);
+    const size_t scratch = scratch_bytes(forest->f, static_cast<long long>(batch));
     void* tmp = nullptr;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (scratch && !ok(cudaMallocAsync(&tmp, scratch, st), "cudaMallocAsync", e)) {

@@ -165,6 +165,10 @@ class Reference:
             lib.montlok_last_error.restype = ctypes.c_char_p
             lib.montlok_set_threads.argtypes = [ctypes.c_int]
             lib.montlok_threads.restype = ctypes.c_int
+            lib.ref_time_calls.restype = ctypes.c_int
+            lib.ref_time_calls.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                                           ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                           ctypes.c_void_p]
             Reference._lib = lib
         self.lib = Reference._lib
 
@@ -204,6 +208,21 @@ class Reference:
         status = self.lib.montlok_model_predict(h, dtype, x.ctypes.data, len(x), out.ctypes.data)
         if status:
             raise RuntimeError(f"reference predict failed ({status}): {self.lib.montlok_last_error().decode()}")
+
+    def time_calls(self, h: ctypes.c_void_p, rows: np.ndarray, batch: int, iterations: int,
+                   warmup: int) -> np.ndarray:
+        """Nanoseconds of each of `iterations` predict calls of `batch` rows
+        (float64 rows [count, batch * features] used in turn), after
+        `warmup` untimed calls; the loop runs in C (ref_timer.c)."""
+        rows = np.ascontiguousarray(rows, dtype=np.float64)
+        features = rows.shape[1] // batch
+        out = np.empty((batch, 64), dtype=np.float64)
+        samples = np.empty(iterations, dtype=np.float64)
+        status = self.lib.ref_time_calls(h, rows.ctypes.data, rows.shape[0], batch, features, iterations, warmup,
+                                         out.ctypes.data, samples.ctypes.data)
+        if status:
+            raise RuntimeError(f"reference predict failed ({status}): {self.lib.montlok_last_error().decode()}")
+        return samples
 
     def leaves(self, model: bytes, x, chunk: int = 4096) -> np.ndarray:
         """Leaf node index per (row, tree) as the reference selects them."""

@@ -94,6 +94,37 @@ def test_ragged_batches(gpu, rows):
     check(model, edge_inputs(rng, rows, 4))
 
 
+SMALL_MODELS = {
+    # complete depth-8 trees, float32 leaves, preprocess: the latency recipe
+    "c5": lambda: synth.model_c5(trees=1000).to_bytes(),
+    # float64 features (ties decided on the doubles), every missing mode, 70 trees: a partial last block
+    "f64_edges": lambda: random_model(np.random.default_rng(31), features=7, trees=70, inf_thresholds=0.1),
+    # float32 features, `lt`, 33 trees: the second CTA of the only block has one tree
+    "f32_lt_33": lambda: random_model(np.random.default_rng(32), features=6, trees=33, decision="lt", cast="f32"),
+    # mean of 130 trees, float64 leaves
+    "mean_130": lambda: random_model(np.random.default_rng(33), features=5, trees=130, aggregate="mean", base=0.5),
+    # fewer trees than a CTA takes
+    "tiny_5": lambda: random_model(np.random.default_rng(34), features=4, trees=5, link="sigmoid"),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SMALL_MODELS))
+@pytest.mark.parametrize("rows", [1, 8, 31, 32, 33, 64])
+def test_small_batches_tree_parallel(gpu, name, rows):
+    """Batches of at most 64 rows on complete-tree models take the
+    tree-parallel kernel (one CTA per 32 trees, block sums by the last CTA of
+    each block, the link by the last block)."""
+    model = SMALL_MODELS[name]()
+    m = montlok.load(model)
+    rng = np.random.default_rng(rows)
+    x = synth.inputs_c5(batch=rows) if name == "c5" else edge_inputs(rng, rows, m.features, 0.2)
+    check(model, x, leaves=rows <= 8)
+    x32 = np.ascontiguousarray(x, dtype=np.float32)
+    assert same_bits(m.predict(x32).reshape(rows, -1), Oracle(model).predict(x32))
+    # The same rows twice in a row: the per-launch counters start from zero again.
+    assert same_bits(m.predict(x).reshape(rows, -1), Oracle(model).predict(x))
+
+
 def test_single_row_and_empty_batch(gpu):
     rng = np.random.default_rng(2)
     model = random_model(rng, features=5, trees=30)
