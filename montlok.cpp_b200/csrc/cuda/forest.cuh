@@ -39,12 +39,30 @@ struct HeapArgs {
     int* status;
 };
 
+// Multi-output layout (sparse_kernels.cu); teams 0 when the model has none.
+struct SparseArgs {
+    int teams;                   // outputs: one team of `rows` threads per output
+    int rows;                    // rows per CTA
+    int leaf32;
+    int slot_bits;               // low bits of a split word: slot << 1 | missing-goes-right
+    int node_max;                // nodes per tree record
+    int record;                  // bytes per tree record
+    int slots;                   // key table rows: (feature, missing kind) pairs and the pad slot
+    int pad_slot;                // slot whose key is always 0 (leaves)
+    int offset[8];               // first record of output k's trees
+    int chunks[8];               // chunks of output k
+    const unsigned char* trees;  // records, output by output, each padded to whole chunks
+    const int* node_ids;         // [records * node_max]: file node of each split, -1 for leaves
+    const int2* slot_of;         // [F]: slot of (feature, NaN missing), (feature, NaN or zero missing)
+};
+
 struct DevForest {
     unsigned long long uid = 0;  // distinct for every forest uploaded by this process
     int device = 0;
     int sm_count = 0;
     ForestArgs args{};
     HeapArgs heap{};
+    SparseArgs sparse{};
     int* status_host = nullptr;  // the status word as the host sees it
     void* blocks[20] = {};  // device allocations, freed with the forest
     int nblocks = 0;
@@ -81,6 +99,13 @@ bool launch_latency(const DevForest& f, int dtype, const void* x, long long batc
                     std::string& err, void* scratch);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
+
+// Multi-output kernel: trees per chunk, rows per CTA that fit (false: none),
+// launch.
+int sparse_chunk_trees();
+bool sparse_plan(int slots, int teams, int record, int& rows);
+bool launch_sparse(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
+                   std::string& err);
 
 }  // namespace mlk::cuda
 

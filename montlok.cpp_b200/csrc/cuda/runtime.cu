@@ -402,6 +402,165 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     return 0;
 }
 
+// Builds and uploads the multi-output records of `v` into f.sparse (left
+// unset, teams 0, when the model does not fit the kernel). A split reads the
+// key of (feature, missing kind): kind 1 for LightGBM's zero missing type,
+// kind 0 otherwise; missing values go right (c = 1) for the NaN-right and
+// zero-right variants. False only on a CUDA error.
+bool upload_sparse(const mlk_forest_view* v, DevForest& f, std::string& e) {
+    const int F = v->features, K = v->outputs, T = v->trees;
+    // Variant slot -> (feature, variant).
+    std::vector<int> slot_feature(static_cast<size_t>(v->slots), -1), slot_variant(static_cast<size_t>(v->slots), -1);
+    for (int feat = 0; feat < F; ++feat) {
+        for (int var = 0; var < 4; ++var) {
+            const int s = v->slot_of[feat * 4 + var];
+            if (s >= 0) {
+                slot_feature[static_cast<size_t>(s)] = feat;
+                slot_variant[static_cast<size_t>(s)] = var;
+            }
+        }
+    }
+    // (feature, kind) slots in kind-major order, then the pad slot.
+    std::vector<int2> slot_of(static_cast<size_t>(F), make_int2(-1, -1));
+    int slots = 0;
+    for (int kind = 0; kind < 2; ++kind) {
+        for (int feat = 0; feat < F; ++feat) {
+            bool used = false;
+            for (int var = 2 * kind; var < 2 * kind + 2; ++var) used = used || v->slot_of[feat * 4 + var] >= 0;
+            if (used) (kind ? slot_of[static_cast<size_t>(feat)].y : slot_of[static_cast<size_t>(feat)].x) = slots++;
+        }
+    }
+    const int pad = slots++;
+    const int slot_bits = heap_slot_bits(2 * slots);
+    const uint32_t mask = (1u << slot_bits) - 1u;
+    // Breadth-first layout of every tree, children of a split adjacent.
+    struct Laid {
+        std::vector<int32_t> order;  // file node of each position
+        std::vector<int32_t> rel;    // positions to the left child, 0 for leaves
+        int leaves = 0;
+    };
+    std::vector<Laid> laid(static_cast<size_t>(T));
+    int node_max = 1, leaf_max = 1;
+    bool f32 = true;
+    constexpr size_t kMaxNodes = 1 << 16;
+    for (int t = 0; t < T; ++t) {
+        Laid& l = laid[static_cast<size_t>(t)];
+        l.order.push_back(v->roots[t]);
+        for (size_t i = 0; i < l.order.size(); ++i) {
+            const int node = l.order[i];
+            if (v->feature[node] >= 0) {
+                l.rel.push_back(static_cast<int32_t>(l.order.size() - i));
+                l.order.push_back(v->node_words[static_cast<size_t>(node) * 4 + 2]);
+                l.order.push_back(v->node_words[static_cast<size_t>(node) * 4 + 3]);
+                if (l.order.size() > kMaxNodes) return true;  // shared subtrees unfolded too far: no sparse view
+            } else {
+                l.rel.push_back(0);
+                ++l.leaves;
+                const double value = v->leaf_value[node];
+                f32 = f32 && static_cast<double>(static_cast<float>(value)) == value;
+            }
+        }
+        node_max = std::max(node_max, static_cast<int>(l.order.size()));
+        leaf_max = std::max(leaf_max, l.leaves);
+    }
+    if (static_cast<uint64_t>(leaf_max + 1) >= (uint64_t{1} << (32 - slot_bits))) return true;
+    const int record = (16 + node_max * 8 + leaf_max * (f32 ? 4 : 8) + 15) & ~15;
+    int rows = 0;
+    if (!sparse_plan(slots, K, record, rows)) return true;
+    // Records output by output, each list padded to whole chunks.
+    const int chunk = sparse_chunk_trees();
+    std::vector<std::vector<int>> lists(static_cast<size_t>(K));
+    for (int t = 0; t < T; ++t) lists[static_cast<size_t>(v->tree_output[t])].push_back(t);
+    SparseArgs& s = f.sparse;
+    int records = 0;
+    for (int k = 0; k < K; ++k) {
+        s.offset[k] = records;
+        const int n = static_cast<int>(lists[static_cast<size_t>(k)].size());
+        s.chunks[k] = (n + chunk - 1) / chunk;
+        records += s.chunks[k] * chunk;
+    }
+    std::vector<unsigned char> host(static_cast<size_t>(records) * record, 0);
+    std::vector<int32_t> ids(static_cast<size_t>(records) * node_max, -1);
+    const uint32_t leaf_low = static_cast<uint32_t>(pad) << 1;
+    for (int k = 0; k < K; ++k) {
+        const auto& list = lists[static_cast<size_t>(k)];
+        for (int j = 0; j < s.chunks[k] * chunk; ++j) {
+            const size_t at = static_cast<size_t>(s.offset[k] + j);
+            unsigned char* rec = host.data() + at * record;
+            int32_t* hdr = reinterpret_cast<int32_t*>(rec);
+            uint32_t* nodes = reinterpret_cast<uint32_t*>(rec + 16);
+            unsigned char* leaves = rec + 16 + static_cast<size_t>(node_max) * 8;
+            if (j >= static_cast<int>(list.size())) {  // inert: one leaf of 0.0, never added
+                nodes[0] = (1u << slot_bits) | leaf_low;
+                continue;
+            }
+            const int t = list[static_cast<size_t>(j)];
+            const Laid& l = laid[static_cast<size_t>(t)];
+            hdr[0] = t / 64;
+            hdr[1] = v->depth[t];
+            hdr[2] = 1;
+            int leaf = 0;
+            for (size_t i = 0; i < l.order.size(); ++i) {
+                const int node = l.order[i];
+                if (v->feature[node] >= 0) {
+                    const int32_t* w = &v->node_words[static_cast<size_t>(node) * 4];
+                    const int var = slot_variant[static_cast<size_t>(w[1])];
+                    const int feat = slot_feature[static_cast<size_t>(w[1])];
+                    const int2 fs = slot_of[static_cast<size_t>(feat)];
+                    const int sl = var >= 2 ? fs.y : fs.x;
+                    const uint32_t c = (var == 0 || var == 2) ? 1u : 0u;  // NaN-right, zero-right
+                    nodes[2 * i] = ((static_cast<uint32_t>(w[0]) ^ 0x80000000u) & ~mask) |
+                                   (static_cast<uint32_t>(sl) << 1) | c;
+                    nodes[2 * i + 1] = static_cast<uint32_t>(l.rel[i]) * 8u;
+                    ids[at * node_max + i] = node;
+                } else {
+                    nodes[2 * i] = (static_cast<uint32_t>(leaf + 1) << slot_bits) | leaf_low;
+                    nodes[2 * i + 1] = 0u;
+                    const double value = v->leaf_value[node];
+                    if (f32) {
+                        const float fv = static_cast<float>(value);
+                        std::memcpy(leaves + static_cast<size_t>(leaf) * 4, &fv, 4);
+                    } else {
+                        std::memcpy(leaves + static_cast<size_t>(leaf) * 8, &value, 8);
+                    }
+                    ++leaf;
+                }
+            }
+        }
+    }
+    void* trees = nullptr;
+    void* dids = nullptr;
+    void* dslots = nullptr;
+    if (!device_alloc(&trees, host.size(), e) ||
+        !ok(cudaMemcpy(trees, host.data(), host.size(), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&dids, ids.size() * 4, e) ||
+        !ok(cudaMemcpy(dids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&dslots, slot_of.size() * sizeof(int2), e) ||
+        !ok(cudaMemcpy(dslots, slot_of.data(), slot_of.size() * sizeof(int2), cudaMemcpyHostToDevice), "cudaMemcpy",
+            e)) {
+        if (trees) cudaFree(trees);
+        if (dids) cudaFree(dids);
+        if (dslots) cudaFree(dslots);
+        s = SparseArgs{};
+        return false;
+    }
+    f.blocks[f.nblocks++] = trees;
+    f.blocks[f.nblocks++] = dids;
+    f.blocks[f.nblocks++] = dslots;
+    s.teams = K;
+    s.rows = rows;
+    s.leaf32 = f32;
+    s.slot_bits = slot_bits;
+    s.node_max = node_max;
+    s.record = record;
+    s.slots = slots;
+    s.pad_slot = pad;
+    s.trees = static_cast<const unsigned char*>(trees);
+    s.node_ids = static_cast<const int*>(dids);
+    s.slot_of = static_cast<const int2*>(dslots);
+    return true;
+}
+
 }  // namespace
 }  // namespace mlk::cuda
 
@@ -608,6 +767,15 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         f.heap.slot_bits = slot_bits;
         f.heap.trees = static_cast<const unsigned char*>(trees);
         f.heap.node_ids = static_cast<const int*>(ids);
+    }
+    // Multi-output records (sparse_kernels.cu) for 2..8 outputs.
+    if (f.heap.depth == 0 && v->outputs >= 2 && v->outputs <= 8 && T > 0) {
+        if (!upload_sparse(v, f, e)) {
+            cudaFreeHost(status);
+            for (int i = 0; i < f.nblocks; ++i) cudaFree(f.blocks[i]);
+            put_error(err, errlen, e);
+            return kInternal;
+        }
     }
     if (!prepare_kernels(f, e)) {
         cudaFreeHost(status);

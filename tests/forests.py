@@ -15,7 +15,7 @@ SPECIALS = [np.nan, 0.0, -0.0, 1e-35, -1e-36, 1e-36, np.inf, -np.inf, 1e-300, -1
 def random_model(rng: np.random.Generator, features: int = 5, decision: str = "le", cast: str = "f64",
                  trees: int = 40, outputs: int = 1, link: str = "identity", aggregate: str = "sum",
                  max_depth: int = 8, inf_thresholds: float = 0.0, base=0.25, sigmoid_scale: float = 1.0,
-                 preprocess=None, share: bool = False) -> bytes:
+                 preprocess=None, share: bool = False, tree_outputs=None) -> bytes:
     """Trees of random depth; every split a random feature, threshold (grid or
     normal, optionally infinite), default side and missing mode."""
     nodes = export.Nodes()
@@ -41,7 +41,8 @@ def random_model(rng: np.random.Generator, features: int = 5, decision: str = "l
         roots.append(grow(0))
     if share and len(roots) > 1:
         roots[-1] = roots[0]
-    tree_outputs = [t % outputs for t in range(trees)]
+    if tree_outputs is None:
+        tree_outputs = [t % outputs for t in range(trees)]
     return export.tree_ensemble(nodes, roots, tree_outputs, features=features, outputs=outputs, decision=decision,
                                 feature_cast=cast, aggregate=aggregate, link=link, base_score=base,
                                 sigmoid_scale=sigmoid_scale, preprocess=preprocess).to_bytes()

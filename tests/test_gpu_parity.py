@@ -71,6 +71,28 @@ def test_links_outputs_and_aggregates(gpu, link, outputs, aggregate):
     check(model, edge_inputs(rng, 400, 6, special=0.2))
 
 
+@pytest.mark.parametrize("outputs", [2, 5, 8])
+@pytest.mark.parametrize("cast, decision", [("f64", "le"), ("f32", "lt")])
+def test_multi_output_kernel(gpu, outputs, cast, decision):
+    """2..8 outputs take the per-output team kernel. Outputs are assigned to
+    trees at random, so some 64-tree blocks hold no tree of an output (whose
+    sum then adds a 0.0 partial, turning -0.0 into +0.0 as the reference
+    does); every missing mode, infinite thresholds, deep trees."""
+    rng = np.random.default_rng([outputs, len(cast), len(decision)])
+    trees = 300
+    tree_outputs = list(rng.integers(0, outputs, size=trees))
+    tree_outputs[:outputs] = range(outputs)
+    for link, aggregate in (("softmax", "sum"), ("identity", "mean")):
+        model = random_model(rng, features=9, trees=trees, outputs=outputs, link=link, aggregate=aggregate,
+                             decision=decision, cast=cast, max_depth=12, inf_thresholds=0.05,
+                             base=list(rng.normal(size=outputs)), tree_outputs=tree_outputs)
+        check(model, edge_inputs(rng, 700, 9, special=0.3))
+    # An output whose trees all sit in block 0, followed by blocks without it.
+    tree_outputs = [0] * 10 + [1] * 150
+    model = random_model(rng, features=5, trees=160, outputs=2, base=[-0.0, 0.5], tree_outputs=tree_outputs)
+    check(model, edge_inputs(rng, 300, 5))
+
+
 @pytest.mark.parametrize("cast", ["f64", "f32"])
 def test_preprocess_then_cast(gpu, cast):
     rng = np.random.default_rng(5)
