@@ -370,10 +370,9 @@ def main() -> None:
     if not np.array_equal(out_np.view(np.int64), y_dev.view(np.int64)):
         raise SystemExit("host-buffer and device-buffer predictions differ")
 
-    worst = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = (float(v) for v in worst.tolist())
+    from montlok.distributed import max_over_ranks
+
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], device="cuda")
 
     if rank == 0:
         peak, peak_kind = peaks()
