@@ -49,7 +49,11 @@ for _p in (ROOT / "montlok.cpp_b200" / "python", ROOT / "oracle"):
 import numpy as np  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
-METRIC = "rows/s (500-tree depth-8 GBDT, 1M rows)"
+METRIC = "rows/s (500-tree depth-8 GBDT, 1M rows)"  # BASELINE.json's metric, quoted on c2
+
+
+def metric_of(cfg) -> str:
+    return METRIC if cfg.name == "c2" else f"rows/s ({cfg.name}: {cfg.describe})"
 
 
 def peaks() -> tuple[float, str]:
@@ -59,12 +63,13 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_per_launch(config: str) -> float | None:
-    """DRAM bytes per launch of the predict kernel from the committed ncu summary."""
+def traffic_per_launch(config: str, rows: int) -> float | None:
+    """DRAM bytes of one launch over `rows` rows, from the committed ncu
+    capture of the same kernel (bytes per row times rows)."""
     path = ROOT / "profiles" / f"{config}_dram_traffic.json"
     if not path.exists():
         return None
-    return float(json.loads(path.read_text())["dram_bytes_per_launch"])
+    return float(json.loads(path.read_text())["dram_bytes_per_row"]) * rows
 
 
 class Clocks:
@@ -165,7 +170,7 @@ def run_reference(args, cfg, model: bytes, x: np.ndarray) -> dict:
         step()
     elapsed = time.perf_counter() - t0
     value = rows * args.steps / elapsed
-    return {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+    return {"metric": metric_of(cfg), "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
             "config": workload(cfg, args),
@@ -378,9 +383,9 @@ def main() -> None:
         peak, peak_kind = peaks()
         bytes_per_launch = batch * F * 8
         achieved = bytes_per_launch / (ms / 1e3) / 1e9
-        traffic = traffic_per_launch(args.config)
+        traffic = traffic_per_launch(args.config, batch)
         line = {
-            "metric": METRIC, "value": world * batch / (ms / 1e3), "unit": "rows/s", "n_gpus": world,
+            "metric": metric_of(cfg), "value": world * batch / (ms / 1e3), "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": workload(cfg, args),

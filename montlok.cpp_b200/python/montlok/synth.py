@@ -32,6 +32,7 @@ keeps every child after its parent as the file format requires.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Callable
 
@@ -122,74 +123,106 @@ def _leafwise(rng: np.random.Generator, trees: int, leaves: int, max_depth: int,
     return nodes, np.asarray(roots, dtype=np.int32)
 
 
+_SAMPLE: tuple | None = None  # (x, y) of the forest being grown, set once per worker process
+
+
+def _set_sample(x: np.ndarray, y: np.ndarray) -> None:
+    global _SAMPLE
+    _SAMPLE = (x, y)
+
+
+def _grow(seed: list, features: int, max_depth: int, min_leaf: int) -> tuple:
+    """One random-split tree on the sample set by _set_sample, from its own
+    seed: (feature, threshold, child, value) arrays in breadth-first order."""
+    x, y = _SAMPLE
+    rng = np.random.default_rng(seed)
+    samples = len(x)
+    cap = 4 * samples
+    feat = np.full(cap, -1, dtype=np.int64)
+    thr = np.zeros(cap)
+    kid = np.full(cap, -1, dtype=np.int64)
+    val = np.zeros(cap)
+    count = 1
+    live = np.arange(samples)
+    at = np.zeros(samples, dtype=np.int64)
+    first, width = 0, 1
+    for level in range(max_depth + 1):
+        local = at[live] - first
+        n_at = np.bincount(local, minlength=width)
+        y_at = np.bincount(local, weights=y[live], minlength=width)
+        val[first:first + width] = y_at / np.maximum(n_at, 1)
+        can = (n_at >= 2 * min_leaf) & (level < max_depth)
+        if not can.any():
+            break
+        choice = rng.integers(0, features, size=width)
+        keep = can[local]
+        live, local = live[keep], local[keep]
+        v = x[live, choice[local]]
+        order = np.lexsort((v, local))
+        live, local, v = live[order], local[order], v[order]
+        split = np.flatnonzero(can)
+        n = n_at[split]
+        starts = np.concatenate([[0], np.cumsum(n)])[:-1]
+        k = min_leaf + np.floor(rng.random(len(split)) * (n - 2 * min_leaf + 1)).astype(np.int64)
+        lo = v[starts + k - 1].astype(np.float64)
+        hi = v[starts + k].astype(np.float64)
+        ok = hi > lo  # equal neighbours cannot be separated: that node stays a leaf
+        good = split[ok]
+        if len(good) == 0:
+            break
+        mid = (lo + (hi - lo) / 2.0)[ok]
+        children = count + 2 * np.arange(len(good))
+        feat[first + good] = choice[good]
+        thr[first + good] = mid
+        kid[first + good] = children
+        child_of = np.full(width, -1, dtype=np.int64)
+        child_of[good] = children
+        thr_of = np.full(width, np.inf)
+        thr_of[good] = mid
+        c = child_of[local]
+        moving = c >= 0
+        at[live[moving]] = c[moving] + (v[moving] > thr_of[local[moving]])
+        live = live[moving]
+        first, width = count, 2 * len(good)
+        count += width
+    return feat[:count], thr[:count], kid[:count], val[:count]
+
+
 def _forest(rng: np.random.Generator, trees: int, samples: int, features: int, max_depth: int,
-            min_leaf: int = 2) -> tuple[dict, np.ndarray]:
+            min_leaf: int = 2, seed: int = MODEL_SEED) -> tuple[dict, np.ndarray]:
     """Random-split regression trees grown breadth-first on a N(0, 1) sample:
     each node of >= 2 * min_leaf samples above the depth limit splits a random
     feature between two adjacent sorted sample values (their midpoint, in
     float64 of float32 features, as scikit-learn does), with a random number of
     samples in [min_leaf, n - min_leaf] on the left. Leaves hold the mean target
-    of their samples."""
+    of their samples. Tree t draws from its own seed (seed, 3, t), so large
+    forests grow in parallel worker processes (started with spawn, which is
+    safe after CUDA was initialised) with the same result."""
     x = rng.standard_normal((samples, features)).astype(np.float32)
     y = np.sin(x[:, 0]) + 0.5 * x[:, 1] * x[:, 2] + 0.1 * rng.standard_normal(samples)
+    seeds = [[seed, 3, t] for t in range(trees)]
+    workers = min(trees, os.cpu_count() or 1)
+    if workers > 1 and trees * samples >= 4_000_000:
+        import multiprocessing
+        from concurrent.futures import ProcessPoolExecutor
+
+        with ProcessPoolExecutor(workers, mp_context=multiprocessing.get_context("spawn"), initializer=_set_sample,
+                                 initargs=(x, y)) as pool:
+            grown = list(pool.map(_grow, seeds, [features] * trees, [max_depth] * trees, [min_leaf] * trees))
+    else:
+        _set_sample(x, y)
+        grown = [_grow(sd, features, max_depth, min_leaf) for sd in seeds]
     parts: dict[str, list] = {k: [] for k in ("feature", "threshold", "left", "right", "value", "flags")}
     roots, total = [], 0
-    for _ in range(trees):
-        cap = 4 * samples
-        feat = np.full(cap, -1, dtype=np.int64)
-        thr = np.zeros(cap)
-        kid = np.full(cap, -1, dtype=np.int64)
-        val = np.zeros(cap)
-        count = 1
-        live = np.arange(samples)
-        at = np.zeros(samples, dtype=np.int64)
-        first, width = 0, 1
-        for level in range(max_depth + 1):
-            local = at[live] - first
-            n_at = np.bincount(local, minlength=width)
-            y_at = np.bincount(local, weights=y[live], minlength=width)
-            val[first:first + width] = y_at / np.maximum(n_at, 1)
-            can = (n_at >= 2 * min_leaf) & (level < max_depth)
-            if not can.any():
-                break
-            choice = rng.integers(0, features, size=width)
-            keep = can[local]
-            live, local = live[keep], local[keep]
-            v = x[live, choice[local]]
-            order = np.lexsort((v, local))
-            live, local, v = live[order], local[order], v[order]
-            split = np.flatnonzero(can)
-            n = n_at[split]
-            starts = np.concatenate([[0], np.cumsum(n)])[:-1]
-            k = min_leaf + np.floor(rng.random(len(split)) * (n - 2 * min_leaf + 1)).astype(np.int64)
-            lo = v[starts + k - 1].astype(np.float64)
-            hi = v[starts + k].astype(np.float64)
-            ok = hi > lo  # equal neighbours cannot be separated: that node stays a leaf
-            good = split[ok]
-            if len(good) == 0:
-                break
-            mid = (lo + (hi - lo) / 2.0)[ok]
-            children = count + 2 * np.arange(len(good))
-            feat[first + good] = choice[good]
-            thr[first + good] = mid
-            kid[first + good] = children
-            child_of = np.full(width, -1, dtype=np.int64)
-            child_of[good] = children
-            thr_of = np.full(width, np.inf)
-            thr_of[good] = mid
-            c = child_of[local]
-            moving = c >= 0
-            at[live[moving]] = c[moving] + (v[moving] > thr_of[local[moving]])
-            live = live[moving]
-            first, width = count, 2 * len(good)
-            count += width
+    for feat, thr, kid, val in grown:
+        count = len(feat)
         roots.append(total)
-        is_split = feat[:count] >= 0
-        parts["feature"].append(feat[:count].astype(np.int32))
-        parts["threshold"].append(thr[:count])
-        parts["left"].append(np.where(is_split, kid[:count] + total, -1).astype(np.int32))
-        parts["right"].append(np.where(is_split, kid[:count] + 1 + total, -1).astype(np.int32))
-        parts["value"].append(np.where(is_split, 0.0, val[:count]))
+        is_split = feat >= 0
+        parts["feature"].append(feat.astype(np.int32))
+        parts["threshold"].append(thr)
+        parts["left"].append(np.where(is_split, kid + total, -1).astype(np.int32))
+        parts["right"].append(np.where(is_split, kid + 1 + total, -1).astype(np.int32))
+        parts["value"].append(np.where(is_split, 0.0, val))
         parts["flags"].append(np.where(is_split, 1 | (_DEFAULT << 1), 0).astype(np.uint8))
         total += count
     nodes = {k: np.concatenate(v) for k, v in parts.items()}
