@@ -111,24 +111,31 @@ class Clocks:
                 "samples": len(rows)}
 
 
+def outputs_of(model: bytes) -> int:
+    from montlok import export
+
+    return int(export.read(model)[0]["outputs"]["size"])
+
+
 def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int) -> tuple[float, str, str]:
     """rows/s of the reference CPU runtime (or the oracle port when the
     reference library is absent) on a bounded sample of `x`."""
     import oracle
 
+    K = outputs_of(model)
     if oracle.available_reference():
         ref = oracle.Reference()
         ref.set_threads(threads)
         h = ref.open(model)
         try:
             probe = x[:8192]
-            out = np.empty((len(probe), 1))
+            out = np.empty((len(probe), K))
             t0 = time.perf_counter()
             ref.predict_handle(h, probe, out)
             rate = len(probe) / max(time.perf_counter() - t0, 1e-9)
             rows = int(min(len(x), max(8192, rate * seconds)))
             sample = np.ascontiguousarray(x[:rows])
-            out = np.empty((rows, 1))
+            out = np.empty((rows, K))
             t0 = time.perf_counter()
             ref.predict_handle(h, sample, out)
             elapsed = time.perf_counter() - t0
@@ -153,7 +160,7 @@ def run_reference(args, cfg, model: bytes, x: np.ndarray) -> dict:
     threads = os.cpu_count() or 1
     rows = min(len(x), args.reference_rows)
     sample = np.ascontiguousarray(x[:rows])
-    out = np.empty((rows, 1))
+    out = np.empty((rows, outputs_of(model)))
     kind = "reference" if oracle.available_reference() else "port"
     if kind == "reference":
         ref = oracle.Reference()

@@ -689,12 +689,15 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
                  std::string& err) {
     const HeapArgs& h = f.heap;
     const bool f64 = dtype == 2;
-    void* k = pick_heap(h.depth, h.rows, h.leaf32, f64);
+    // Fewer rows per CTA while the batch would leave SMs idle.
+    int rows = h.rows;
+    while (rows > 32 && (batch + rows - 1) / rows < f.sm_count) rows /= 2;
+    void* k = pick_heap(h.depth, rows, h.leaf32, f64);
     if (!k) {
         err = "no complete-tree kernel for this model";
         return false;
     }
-    const int smem = layout_of(f.args.slots, h.depth, h.leaf32, h.rows).total;
+    const int smem = layout_of(f.args.slots, h.depth, h.leaf32, rows).total;
     {
         static std::mutex mu;
         static std::vector<std::pair<void*, int>> set;
@@ -708,13 +711,14 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
             set.emplace_back(k, f.device);
         }
     }
-    const long long groups = (batch + h.rows - 1) / h.rows;
+    const long long groups = (batch + rows - 1) / rows;
     const int per_sm = std::max(1, kHeapSmemLimit / (smem + 1024));
     const int grid = static_cast<int>(std::min<long long>(groups, static_cast<long long>(f.sm_count) * per_sm));
     ForestArgs a = f.args;
     HeapArgs hh = h;
+    hh.rows = rows;
     void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out};
-    const cudaError_t e = cudaLaunchKernel(k, grid, kTeams * h.rows, args, smem, stream);
+    const cudaError_t e = cudaLaunchKernel(k, grid, kTeams * rows, args, smem, stream);
     if (e != cudaSuccess) {
         err = std::string("complete-tree kernel launch: ") + cudaGetErrorString(e);
         return false;

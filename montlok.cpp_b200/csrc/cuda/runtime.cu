@@ -162,7 +162,10 @@ struct CachedGraph {
     int dtype = 0;
     size_t batch = 0;
     const void* buffers[5] = {};
+    cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    cudaGraphNode_t input_copy = nullptr;  // the host -> device copy, re-pointed at pinned caller inputs
+    const void* input = nullptr;           // where that copy reads now
     unsigned long long used = 0;
 };
 
@@ -175,6 +178,7 @@ struct Workspace {
     ~Workspace() {
         for (auto& g : graphs) {
             if (g.exec) cudaGraphExecDestroy(g.exec);
+            if (g.graph) cudaGraphDestroy(g.graph);
         }
         for (auto s : stream) {
             if (s) cudaStreamDestroy(s);
@@ -199,10 +203,11 @@ constexpr size_t kGraphRows = 4096;  // host-buffer predicts of at most this man
 constexpr size_t kGraphCache = 8;    // graphs kept per workspace
 
 // A predict of at most kGraphRows rows from and to host memory: the input is
-// copied into the workspace's pinned staging buffer, a cached graph of
-// (host -> device copy, kernel) runs on the workspace's first stream, the
-// kernel storing its results into pinned host memory directly, and the
-// result is copied out. The graph is captured on the first call with this
+// copied into the workspace's pinned staging buffer (or, when the caller's
+// input is pinned already, the graph's copy reads it in place), a cached
+// graph of (host -> device copy, kernel) runs on the workspace's first
+// stream, the kernel storing its results into pinned host memory directly,
+// and the result is copied out. The graph is captured on the first call with this
 // forest, input type and row count (or after a staging buffer grew), so
 // later calls of the same shape pay one graph launch instead of separate
 // stream operations and kernel launches.
@@ -248,13 +253,27 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
             if (good) good = ok(end, "cudaStreamEndCapture", e);
             cudaGraphExec_t exec = nullptr;
             if (good) good = ok(cudaGraphInstantiate(&exec, graph, 0), "cudaGraphInstantiate", e);
-            if (graph) cudaGraphDestroy(graph);
+            cudaGraphNode_t input_copy = nullptr;
+            if (good) {
+                size_t n = 0;
+                cudaGraphGetNodes(graph, nullptr, &n);
+                std::vector<cudaGraphNode_t> nodes(n);
+                if (n && cudaGraphGetNodes(graph, nodes.data(), &n) == cudaSuccess) {
+                    for (auto node : nodes) {
+                        cudaGraphNodeType type;
+                        if (cudaGraphNodeGetType(node, &type) == cudaSuccess && type == cudaGraphNodeTypeMemcpy) {
+                            input_copy = node;
+                        }
+                    }
+                }
+            }
             cudaGetLastError();
             if (good) {
                 if (w->graphs.size() >= kGraphCache) {
                     auto oldest = std::min_element(w->graphs.begin(), w->graphs.end(),
                                                    [](const CachedGraph& a, const CachedGraph& b) { return a.used < b.used; });
                     cudaGraphExecDestroy(oldest->exec);
+                    cudaGraphDestroy(oldest->graph);
                     w->graphs.erase(oldest);
                 }
                 CachedGraph c;
@@ -262,9 +281,14 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
                 c.dtype = dtype;
                 c.batch = batch;
                 std::copy(buffers, buffers + 5, c.buffers);
+                c.graph = graph;
                 c.exec = exec;
+                c.input_copy = input_copy;
+                c.input = w->hx[0].p;
                 w->graphs.push_back(c);
                 g = &w->graphs.back();
+            } else if (graph) {
+                cudaGraphDestroy(graph);
             }
         }
         if (!good) {
@@ -273,7 +297,19 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
         }
     }
     g->used = ++w->tick;
-    std::memcpy(w->hx[0].p, x, in_bytes);
+    int kind = MLK_PTR_PAGEABLE, dev = -1;
+    mlk_cuda_pointer_kind(x, &kind, &dev);
+    const void* src = (kind == MLK_PTR_PINNED && g->input_copy) ? x : w->hx[0].p;
+    if (src != g->input) {
+        if (!ok(cudaGraphExecMemcpyNodeSetParams1D(g->exec, g->input_copy, w->dx[0].p, src, in_bytes,
+                                                   cudaMemcpyHostToDevice),
+                "cudaGraphExecMemcpyNodeSetParams1D", e)) {
+            put_error(err, errlen, e);
+            return kInternal;
+        }
+        g->input = src;
+    }
+    if (src != x) std::memcpy(w->hx[0].p, x, in_bytes);
     bool good = ok(cudaGraphLaunch(g->exec, st), "cudaGraphLaunch", e) &&
                 ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
     if (good) std::memcpy(out, w->hout[0].p, out_bytes);

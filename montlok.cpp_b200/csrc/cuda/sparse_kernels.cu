@@ -465,7 +465,10 @@ bool sparse_plan(int slots, int teams, int record, int& rows) {
 
 bool launch_sparse(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                    std::string& err) {
-    const SparseArgs& s = f.sparse;
+    SparseArgs ss = f.sparse;
+    // Fewer rows per CTA while the batch would leave SMs idle.
+    while (ss.rows > 32 && (batch + ss.rows - 1) / ss.rows < f.sm_count) ss.rows = ss.rows == 96 ? 64 : 32;
+    const SparseArgs& s = ss;
     void* k = pick_sparse(s.teams, s.rows, s.leaf32, dtype == 2);
     if (!k) {
         err = "no multi-output kernel for this model";
@@ -488,7 +491,6 @@ bool launch_sparse(const DevForest& f, int dtype, const void* x, long long batch
     const long long groups = (batch + s.rows - 1) / s.rows;
     const int grid = static_cast<int>(std::min<long long>(groups, static_cast<long long>(f.sm_count)));
     ForestArgs a = f.args;
-    SparseArgs ss = s;
     void* args[] = {&a, &ss, const_cast<void**>(&x), &batch, &out};
     const cudaError_t e = cudaLaunchKernel(k, grid, s.teams * s.rows, args, smem, stream);
     if (e != cudaSuccess) {

@@ -183,6 +183,9 @@ class Reference:
         status = self.lib.montlok_model_open_memory(model, len(model), ctypes.byref(h))
         if status:
             raise ValueError(f"reference rejects the model ({status}): {self.lib.montlok_last_error().decode()}")
+        spec, _ = export.read(model)
+        self._outputs = getattr(self, "_outputs", {})
+        self._outputs[h.value] = int(spec["outputs"]["size"])
         return h
 
     def close(self, h: ctypes.c_void_p) -> None:
@@ -205,6 +208,9 @@ class Reference:
         return out
 
     def predict_handle(self, h: ctypes.c_void_p, x: np.ndarray, out: np.ndarray, dtype: int = 2) -> None:
+        K = getattr(self, "_outputs", {}).get(h.value)
+        if K is None or out.dtype != np.float64 or not out.flags.c_contiguous or out.size != len(x) * K:
+            raise ValueError("out must be a C-contiguous float64 array of rows x outputs")
         status = self.lib.montlok_model_predict(h, dtype, x.ctypes.data, len(x), out.ctypes.data)
         if status:
             raise RuntimeError(f"reference predict failed ({status}): {self.lib.montlok_last_error().decode()}")

@@ -147,6 +147,23 @@ def test_small_batches_tree_parallel(gpu, name, rows):
     assert same_bits(m.predict(x).reshape(rows, -1), Oracle(model).predict(x))
 
 
+def test_small_calls_from_pinned_and_pageable_inputs(gpu):
+    """Small host-buffer calls replay a cached graph whose input copy reads
+    the caller's buffer in place when it is pinned: alternate pinned and
+    pageable inputs of the same shape and check every call's bits."""
+    torch = pytest.importorskip("torch")
+    model = synth.model_c2(trees=130).to_bytes()
+    m, o = montlok.load(model), Oracle(model)
+    for rows in (1, 64, 3000):
+        xs = [synth.inputs_c2(batch=rows + k)[k:] for k in range(3)]
+        pinned = [torch.from_numpy(np.ascontiguousarray(x)).pin_memory() for x in xs]
+        for x, xp in zip(xs, pinned):
+            want = o.predict(x)
+            assert same_bits(m.predict(x).reshape(want.shape), want)
+            assert same_bits(m.predict(xp.numpy()).reshape(want.shape), want)
+        assert same_bits(m.predict(xs[0]).reshape(rows, 1), o.predict(xs[0]))
+
+
 def test_single_row_and_empty_batch(gpu):
     rng = np.random.default_rng(2)
     model = random_model(rng, features=5, trees=30)
