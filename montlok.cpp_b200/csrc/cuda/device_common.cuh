@@ -98,6 +98,64 @@ __device__ void prepare_group(const ForestArgs& a, const XT* __restrict__ x, lon
     __syncwarp();
 }
 
+inline constexpr int kPrepTile = 4;                               // features per transpose tile
+inline constexpr int kPrepTileBytes = 32 * (kPrepTile + 1) * 8;  // one warp's tile
+
+// Keys of the 32 rows row0 .. row0 + 31 for features [f_begin, f_end): the
+// warp reads kPrepTile features of all 32 rows per step (four coalesced loads of
+// 8 rows x kPrepTile values; the next two steps' loads are in flight meanwhile),
+// stages them in `tile` ([32][kPrepTile + 1] doubles) and each lane turns its own
+// row's values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
+template <int STRIDE, typename XT>
+__device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
+                             double* tile, int lane, int f_begin, int f_end, int low) {
+    constexpr int kPerLoad = 32 / kPrepTile;  // rows covered by one warp-wide load
+    const int sub = lane / kPrepTile, f_in = lane % kPrepTile;
+    auto load = [&](int f0, double (&v)[kPrepTile]) {
+        const int feat = f0 + f_in;
+#pragma unroll
+        for (int i = 0; i < kPrepTile; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            v[i] = (feat < f_end && row < batch) ? load_x(x + row * a.F + feat) : 0.0;
+        }
+    };
+    auto stage = [&](int f0, const double (&v)[kPrepTile]) {
+        const int feat = f0 + f_in;
+        double mean = 0.0, scale = 1.0;
+        if (a.standardize && feat < f_end) {
+            mean = __ldg(a.pre_mean + feat);
+            scale = __ldg(a.pre_scale + feat);
+        }
+#pragma unroll
+        for (int i = 0; i < kPrepTile; ++i) {
+            const long long row = row0 + i * kPerLoad + sub;
+            tile[(i * kPerLoad + sub) * (kPrepTile + 1) + f_in] =
+                (feat < f_end && row < batch) ? finish(a, v[i], mean, scale) : 0.0;
+        }
+    };
+    auto keys_of = [&](int f0) {
+        __syncwarp();
+        const int nf = min(kPrepTile, f_end - f0);
+        for (int j = 0; j < nf; ++j) {
+            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kPrepTile + 1) + j], low);
+        }
+        __syncwarp();
+    };
+    double even[kPrepTile], odd[kPrepTile];
+    load(f_begin, even);
+    load(f_begin + kPrepTile, odd);
+    for (int f0 = f_begin; f0 < f_end; f0 += 2 * kPrepTile) {
+        stage(f0, even);
+        load(f0 + 2 * kPrepTile, even);
+        keys_of(f0);
+        if (f0 + kPrepTile < f_end) {
+            stage(f0 + kPrepTile, odd);
+            load(f0 + 3 * kPrepTile, odd);
+            keys_of(f0 + kPrepTile);
+        }
+    }
+}
+
 // The split decided on doubles, for a float64 model whose keys tied.
 template <typename XT>
 __device__ __noinline__ bool exact_right(const ForestArgs& a, const XT* __restrict__ x, long long row,

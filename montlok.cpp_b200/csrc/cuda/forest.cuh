@@ -56,6 +56,16 @@ struct SparseArgs {
     const int2* slot_of;         // [F]: slot of (feature, NaN missing), (feature, NaN or zero missing)
 };
 
+// Deep-tree layout (deep_kernels.cu); nodes null when the model has none.
+struct DeepArgs {
+    int slot_bits;       // low bits of a split word holding the slot
+    int leaf32;          // leaf values are float32
+    const uint2* nodes;  // breadth-first per tree: {word, index of the left child}
+    const void* leaves;  // leaf values, indexed by the leaf number in a leaf's word
+    const int* roots;    // [T]: node index of each tree's root
+    const int* node_ids; // [nodes]: file node of each split, -1 for leaves
+};
+
 struct DevForest {
     unsigned long long uid = 0;  // distinct for every forest uploaded by this process
     int device = 0;
@@ -63,6 +73,7 @@ struct DevForest {
     ForestArgs args{};
     HeapArgs heap{};
     SparseArgs sparse{};
+    DeepArgs deep{};
     int* status_host = nullptr;  // the status word as the host sees it
     void* blocks[20] = {};  // device allocations, freed with the forest
     int nblocks = 0;
@@ -98,6 +109,11 @@ bool latency_fits(const DevForest& f, long long batch);
 bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                     std::string& err, void* scratch);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
+                 std::string& err);
+
+// Deep-tree kernel (one output): whether a model's key tables fit, launch.
+bool deep_fits(int slots);
+bool launch_deep(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
 
 // Multi-output kernel: trees per chunk, rows per CTA that fit (false: none),

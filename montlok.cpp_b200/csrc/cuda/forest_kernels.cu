@@ -259,6 +259,7 @@ bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch
         return launch_heap(f, dtype, x, batch, out, stream, err);
     }
     if (out && !leaves && f.sparse.teams > 0) return launch_sparse(f, dtype, x, batch, out, stream, err);
+    if (out && !leaves && f.deep.nodes) return launch_deep(f, dtype, x, batch, out, stream, err);
     const ForestArgs& a = f.args;
     const Shape s = shape_of(a);
     const bool ties = !a.cast_f32;

@@ -54,8 +54,7 @@ namespace {
 constexpr int kTeams = 4;                              // teams of R threads, one 64-tree block each at a time
 constexpr int kTrees = 4;                              // trees per chunk = trees one thread walks side by side
 constexpr int kChunksPerBlock = kTreeBlock / kTrees;   // 16
-constexpr int kTile = 4;                               // features per transpose tile in the prepare
-constexpr int kTileBytes = 32 * (kTile + 1) * 8;       // one warp's transpose tile
+constexpr int kTileBytes = kPrepTileBytes;            // one warp's transpose tile in the prepare
 constexpr long long kSpinLimit = 1ll << 26;            // mbarrier polls before giving up
 constexpr int kHeapSmemLimit = 227 * 1024;
 constexpr int kMaxSlotBits = 10;
@@ -150,61 +149,6 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
     for (uintptr_t a = lo; a < hi; a += (1u << 20)) {
         const uint32_t n = static_cast<uint32_t>(min(static_cast<uintptr_t>(1u << 20), hi - a));
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
-    }
-}
-
-// Keys of the 32 rows row0 .. row0 + 31 for features [f_begin, f_end): the
-// warp reads kTile features of all 32 rows per step (four coalesced loads of
-// 8 rows x kTile values; the next two steps' loads are in flight meanwhile),
-// stages them in `tile` ([32][kTile + 1] doubles) and each lane turns its own
-// row's values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
-template <int STRIDE, typename XT>
-__device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
-                             double* tile, int lane, int f_begin, int f_end, int low) {
-    constexpr int kPerLoad = 32 / kTile;  // rows covered by one warp-wide load
-    const int sub = lane / kTile, f_in = lane % kTile;
-    auto load = [&](int f0, double (&v)[kTile]) {
-        const int feat = f0 + f_in;
-#pragma unroll
-        for (int i = 0; i < kTile; ++i) {
-            const long long row = row0 + i * kPerLoad + sub;
-            v[i] = (feat < f_end && row < batch) ? load_x(x + row * a.F + feat) : 0.0;
-        }
-    };
-    auto stage = [&](int f0, const double (&v)[kTile]) {
-        const int feat = f0 + f_in;
-        double mean = 0.0, scale = 1.0;
-        if (a.standardize && feat < f_end) {
-            mean = __ldg(a.pre_mean + feat);
-            scale = __ldg(a.pre_scale + feat);
-        }
-#pragma unroll
-        for (int i = 0; i < kTile; ++i) {
-            const long long row = row0 + i * kPerLoad + sub;
-            tile[(i * kPerLoad + sub) * (kTile + 1) + f_in] =
-                (feat < f_end && row < batch) ? finish(a, v[i], mean, scale) : 0.0;
-        }
-    };
-    auto keys_of = [&](int f0) {
-        __syncwarp();
-        const int nf = min(kTile, f_end - f0);
-        for (int j = 0; j < nf; ++j) {
-            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kTile + 1) + j], low);
-        }
-        __syncwarp();
-    };
-    double even[kTile], odd[kTile];
-    load(f_begin, even);
-    load(f_begin + kTile, odd);
-    for (int f0 = f_begin; f0 < f_end; f0 += 2 * kTile) {
-        stage(f0, even);
-        load(f0 + 2 * kTile, even);
-        keys_of(f0);
-        if (f0 + kTile < f_end) {
-            stage(f0 + kTile, odd);
-            load(f0 + 3 * kTile, odd);
-            keys_of(f0 + kTile);
-        }
     }
 }
 

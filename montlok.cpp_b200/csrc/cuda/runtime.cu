@@ -438,6 +438,78 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     return 0;
 }
 
+// Builds and uploads the deep-tree node array of `v` into f.deep (left
+// unset when the leaf numbers do not fit a split word). False only on a CUDA
+// error.
+bool upload_deep(const mlk_forest_view* v, DevForest& f, std::string& e) {
+    const int T = v->trees;
+    const int slot_bits = heap_slot_bits(v->slots);
+    const uint32_t mask = (1u << slot_bits) - 1u;
+    std::vector<uint2> nodes;
+    std::vector<int32_t> ids, roots(static_cast<size_t>(T));
+    std::vector<double> leaves;
+    bool f32 = true;
+    constexpr size_t kMaxNodes = size_t{1} << 31;
+    for (int t = 0; t < T; ++t) {
+        // Breadth first, children adjacent: position i of the tree at base + i.
+        const size_t base = nodes.size();
+        roots[static_cast<size_t>(t)] = static_cast<int32_t>(base);
+        std::vector<int32_t> order{v->roots[t]};
+        for (size_t i = 0; i < order.size(); ++i) {
+            const int node = order[i];
+            if (v->feature[node] >= 0) {
+                const int32_t* w = &v->node_words[static_cast<size_t>(node) * 4];
+                nodes.push_back(make_uint2((static_cast<uint32_t>(w[0]) & ~mask) | static_cast<uint32_t>(w[1]),
+                                           static_cast<uint32_t>(base + order.size())));
+                ids.push_back(node);
+                order.push_back(w[2]);
+                order.push_back(w[3]);
+            } else {
+                const uint64_t leaf = leaves.size() + 1;
+                if (leaf >= (uint64_t{1} << (31 - slot_bits))) return true;  // leaf numbers overflow the word
+                nodes.push_back(make_uint2((static_cast<uint32_t>(leaf) << slot_bits) |
+                                               static_cast<uint32_t>(v->pad_slot),
+                                           static_cast<uint32_t>(base + i)));
+                ids.push_back(-1);
+                const double value = v->leaf_value[node];
+                leaves.push_back(value);
+                f32 = f32 && static_cast<double>(static_cast<float>(value)) == value;
+            }
+            if (nodes.size() >= kMaxNodes) return true;  // shared subtrees unfolded too far
+        }
+    }
+    std::vector<float> leaves32;
+    if (f32) leaves32.assign(leaves.begin(), leaves.end());
+    const size_t leaf_bytes = f32 ? leaves32.size() * 4 : leaves.size() * 8;
+    const void* leaf_src = f32 ? static_cast<const void*>(leaves32.data()) : static_cast<const void*>(leaves.data());
+    void* dnodes = nullptr;
+    void* dleaves = nullptr;
+    void* droots = nullptr;
+    void* dids = nullptr;
+    if (!device_alloc(&dnodes, nodes.size() * sizeof(uint2), e) ||
+        !ok(cudaMemcpy(dnodes, nodes.data(), nodes.size() * sizeof(uint2), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&dleaves, std::max<size_t>(leaf_bytes, 16), e) ||
+        !ok(cudaMemcpy(dleaves, leaf_src, leaf_bytes, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&droots, roots.size() * 4, e) ||
+        !ok(cudaMemcpy(droots, roots.data(), roots.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&dids, ids.size() * 4, e) ||
+        !ok(cudaMemcpy(dids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
+        for (void* p : {dnodes, dleaves, droots, dids}) {
+            if (p) cudaFree(p);
+        }
+        return false;
+    }
+    for (void* p : {dnodes, dleaves, droots, dids}) f.blocks[f.nblocks++] = p;
+    DeepArgs& d = f.deep;
+    d.slot_bits = slot_bits;
+    d.leaf32 = f32;
+    d.nodes = static_cast<const uint2*>(dnodes);
+    d.leaves = dleaves;
+    d.roots = static_cast<const int*>(droots);
+    d.node_ids = static_cast<const int*>(dids);
+    return true;
+}
+
 // Builds and uploads the multi-output records of `v` into f.sparse (left
 // unset, teams 0, when the model does not fit the kernel). A split reads the
 // key of (feature, missing kind): kind 1 for LightGBM's zero missing type,
@@ -803,6 +875,16 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
         f.heap.slot_bits = slot_bits;
         f.heap.trees = static_cast<const unsigned char*>(trees);
         f.heap.node_ids = static_cast<const int*>(ids);
+    }
+    // Deep-tree nodes (deep_kernels.cu) for single-output models the
+    // complete-tree layout does not take.
+    if (f.heap.depth == 0 && v->outputs == 1 && T > 0 && deep_fits(v->slots)) {
+        if (!upload_deep(v, f, e)) {
+            cudaFreeHost(status);
+            for (int i = 0; i < f.nblocks; ++i) cudaFree(f.blocks[i]);
+            put_error(err, errlen, e);
+            return kInternal;
+        }
     }
     // Multi-output records (sparse_kernels.cu) for 2..8 outputs.
     if (f.heap.depth == 0 && v->outputs >= 2 && v->outputs <= 8 && T > 0) {

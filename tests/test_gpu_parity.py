@@ -93,6 +93,22 @@ def test_multi_output_kernel(gpu, outputs, cast, decision):
     check(model, edge_inputs(rng, 300, 5))
 
 
+@pytest.mark.parametrize("cast, decision", [("f64", "le"), ("f32", "lt"), ("f32", "le")])
+@pytest.mark.parametrize("inf", [0.0, 0.1])
+def test_deep_tree_kernel(gpu, cast, decision, inf):
+    """One output, trees deeper than 8 levels: the deep-tree kernel (node
+    array in L2, 8 trees per lane, leaf words naming their values), every
+    missing mode, infinite thresholds, mean and sum, float32 inputs."""
+    rng = np.random.default_rng([len(cast), len(decision), int(inf * 10)])
+    for aggregate, link in (("sum", "sigmoid"), ("mean", "identity")):
+        model = random_model(rng, features=8, trees=150, max_depth=16, cast=cast, decision=decision,
+                             inf_thresholds=inf, aggregate=aggregate, link=link, base=0.3)
+        x = edge_inputs(rng, 900, 8, special=0.3)
+        check(model, x)
+        assert same_bits(montlok.load(model).predict(x.astype(np.float32)).reshape(-1, 1),
+                         Oracle(model).predict(x.astype(np.float32)))
+
+
 @pytest.mark.parametrize("cast", ["f64", "f32"])
 def test_preprocess_then_cast(gpu, cast):
     rng = np.random.default_rng(5)
