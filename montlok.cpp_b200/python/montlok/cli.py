@@ -135,6 +135,7 @@ def cmd_convert(args: argparse.Namespace) -> int:
 
 def cmd_predict(args: argparse.Namespace) -> int:
     montlok.set_threads(args.threads)
+    montlok.set_devices(args.devices)
     model = montlok.load(args.model)
     table, header = read_table(args.input)
     if isinstance(table, dict):
@@ -148,18 +149,58 @@ def _ns(value: float) -> str:
     return f"{value:.0f} ns" if value < 1000 else f"{value / 1000:.2f} µs" if value < 1e6 else f"{value / 1e6:.2f} ms"
 
 
+def bench_device(model, rows: np.ndarray, batch: int, iterations: int) -> tuple[np.ndarray, float]:
+    """Per-call latency of montlok_model_predict_device with inputs and outputs
+    resident on the GPU (CUDA events around each call), and the mean of
+    back-to-back calls."""
+    import torch
+
+    x = torch.from_numpy(np.ascontiguousarray(rows.reshape(-1, model.features))).cuda()
+    out = torch.empty((len(rows) * batch, model.outputs), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.Stream()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iterations)]
+
+    def call(i: int) -> None:
+        j = (i % len(rows)) * batch
+        model.predict_device(x[j].data_ptr(), batch, out[j].data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
+
+    for i in range(max(100, iterations // 10)):
+        call(i)
+    for i, (a, b) in enumerate(events):
+        a.record(stream)
+        call(i)
+        b.record(stream)
+    stream.synchronize()
+    samples = np.array([a.elapsed_time(b) * 1e6 for a, b in events])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(iterations):
+        call(i)
+    end.record(stream)
+    stream.synchronize()
+    return samples, start.elapsed_time(end) * 1e6 / iterations
+
+
 def cmd_bench(args: argparse.Namespace) -> int:
     montlok.set_threads(args.threads)
     montlok.set_latency_threads(args.latency_threads)
+    montlok.set_devices(args.devices)
     try:
         model = montlok.load(args.model)
         rows = np.random.default_rng(7).standard_normal((args.rows, args.batch * model.features))
-        samples, mean = montlok._core.bench(model, rows, args.batch, args.iterations, args.stream)
+        if args.memory == "device":
+            samples, mean = bench_device(model, rows, args.batch, args.iterations)
+        else:
+            if args.memory == "pinned":
+                import torch
+
+                rows = torch.from_numpy(rows).pin_memory().numpy()
+            samples, mean = montlok._core.bench(model, rows, args.batch, args.iterations, args.stream)
     finally:
         montlok.set_latency_threads(0)
     p50, p90, p99, p999 = np.percentile(samples, [50, 90, 99, 99.9])
     call = "stream step" if args.stream else "predict"
-    print(f"{args.model}: {call}, batch {args.batch}, {args.threads} thread(s), "
+    print(f"{args.model}: {call}, batch {args.batch}, {args.memory} memory, {args.threads} thread(s), "
           f"{args.latency_threads} latency thread(s), {args.iterations} calls")
     print(f"p50 {_ns(p50)}  p90 {_ns(p90)}  p99 {_ns(p99)}  p99.9 {_ns(p999)}  mean {_ns(mean)}")
     print(f"{1e9 / mean:,.0f} calls/s, {args.batch * 1e9 / mean:,.0f} rows/s")
@@ -197,6 +238,7 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("input", help="CSV (header optional), .npy or .npz")
     p.add_argument("-o", "--output", help="CSV or .npy (default: CSV on stdout)")
     p.add_argument("--threads", type=int, default=0, help="host staging threads (default: one per hardware thread)")
+    p.add_argument("--devices", type=int, default=0, help="GPUs the rows are split over (default: the current one)")
     p.set_defaults(run=cmd_predict)
     p = commands.add_parser("bench", help="in-process latency of one model")
     p.add_argument("model")
@@ -206,6 +248,9 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--threads", type=int, default=1)
     p.add_argument("--latency-threads", type=int, default=0)
     p.add_argument("--stream", action="store_true", help="time stream steps (stateless for trees)")
+    p.add_argument("--memory", choices=("host", "pinned", "device"), default="host",
+                   help="where inputs and outputs live: pageable host, pinned host, or GPU (predict_device)")
+    p.add_argument("--devices", type=int, default=0, help="GPUs host batches are split over (default: the current one)")
     p.set_defaults(run=cmd_bench)
     p = commands.add_parser("env", help="versions, GPUs and settings")
     p.set_defaults(run=cmd_env)
