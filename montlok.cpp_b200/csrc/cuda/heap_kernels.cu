@@ -181,9 +181,7 @@ template <int D, int R, bool LEAF32, typename XT>
 __device__ __forceinline__ void walk_leaves(const ForestArgs& a, const HeapArgs& h, uint32_t buf, uint32_t col,
                                             uint32_t mask, int tree0, const XT* x, long long row, long long batch,
                                             double (&v)[kTrees]) {
-    constexpr int kSplits = (1 << D) - 1;
     constexpr int kRec = record_bytes(D, LEAF32);
-    constexpr int kLeafBytes = LEAF32 ? 4 : 8;
     uint32_t p[kTrees], go_left[kTrees];
     bool tie[kTrees];
 #pragma unroll
@@ -218,11 +216,12 @@ __device__ __forceinline__ void walk_leaves(const ForestArgs& a, const HeapArgs&
             }
         }
     }
+    // Heap index i >= 2^D - 1 sits at byte base + 4i; its leaf value (leaf
+    // i - (2^D - 1) after the 2^D words) at base + 4i + 4 for float32
+    // leaves, at 2(base + 4i) - base + 8 - 4 * 2^D for float64 ones.
 #pragma unroll
     for (int t = 0; t < kTrees; ++t) {
-        const uint32_t base = buf + t * kRec;
-        const uint32_t leaf = ((p[t] - base) >> 2) - kSplits;
-        v[t] = lds_leaf(base + (4u << D) + leaf * kLeafBytes, LEAF32);
+        v[t] = LEAF32 ? lds_leaf(p[t] + 4u, true) : lds_leaf(2u * p[t] + go_left[t] + (4u - (4u << D)), false);
     }
 }
 
