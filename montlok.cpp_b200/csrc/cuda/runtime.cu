@@ -201,16 +201,15 @@ Workspace* workspace(int device, std::string& err) {
 
 constexpr size_t kGraphRows = 4096;  // host-buffer predicts of at most this many rows replay a graph
 constexpr size_t kGraphCache = 8;    // graphs kept per workspace
-constexpr size_t kZeroCopyRows = 8;  // calls this small skip the input copy
 
 // A predict of at most kGraphRows rows from and to host memory: the input is
 // copied into the workspace's pinned staging buffer (or, when the caller's
 // input is pinned already, the graph's copy reads it in place), a cached
 // graph of (host -> device copy, kernel) runs on the workspace's first
 // stream, the kernel storing its results into pinned host memory directly,
-// and the result is copied out. Calls of at most kZeroCopyRows rows that the
-// small-batch kernel takes have no copy node: that kernel reads the few rows
-// from the pinned staging buffer over the bus. The graph is captured on the first call with this
+// and the result is copied out. (Letting the small-batch kernel read a few
+// rows over the bus instead of copying them was slower: each of its CTAs
+// pays the bus latency.) The graph is captured on the first call with this
 // forest, input type and row count (or after a staging buffer grew), so
 // later calls of the same shape pay one graph launch instead of separate
 // stream operations and kernel launches.
@@ -241,17 +240,14 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
     if (!g) {
         bool good = ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture", e);
         if (good) {
-            // A few rows for the small-batch kernel are read by the kernel
-            // straight from the pinned staging buffer (no copy node).
-            const bool zero_copy = batch <= kZeroCopyRows && latency_fits(f, static_cast<long long>(batch));
-            if (!zero_copy) good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e);
+            good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e);
             if (good && injected("launch")) {
                 e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
                 good = false;
             }
             // The kernel stores the results straight into the pinned staging
             // buffer (host memory the device addresses directly).
-            good = good && launch_forest(f, dtype, zero_copy ? w->hx[0].p : w->dx[0].p, static_cast<long long>(batch),
+            good = good && launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
                                          static_cast<double*>(w->hout[0].p), nullptr, st, e,
                                          static_cast<int*>(w->scratch.p));
             cudaGraph_t graph = nullptr;
