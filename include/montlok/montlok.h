@@ -130,10 +130,12 @@ MONTLOK_API int montlok_model_predict_device(const montlok_model* model, montlok
  * loops whose device memory belongs to another allocator (a framework's
  * caching pool that has already reserved the GPU) and latency-critical paths
  * that must not pay for cudaMalloc/cudaFree or the device-wide
- * synchronisation cudaFree implies. It allocates nothing: the key tables of
- * each 32-row group live in a static 16 MiB device array of this library
- * (present on every GPU that loads it, until the process exits), and the
- * kernel grid is cut to the tables that fit. A model needing more than 16 MiB
+ * synchronisation cudaFree implies. It allocates nothing: models the
+ * complete-tree, multi-output or deep-tree kernels take keep their key tables
+ * in shared memory; for the others the key tables of each 32-row group live
+ * in a static 16 MiB device array of this library (present on every GPU that
+ * loads it, until the process exits), and the kernel grid is cut to the
+ * tables that fit. A model needing more than 16 MiB
  * for one table (more than 131072 feature/missing-rule slots, about 32768
  * features) fails with MONTLOK_ERROR_UNSUPPORTED. The model must already be
  * resident on the current device (after one predict or predict_device call

@@ -361,6 +361,11 @@ bool noalloc_scratch(int device, int** out, std::string& err) {
 int launch_forest_noalloc(const DevForest& f, int dtype, const void* x, long long batch, double* out,
                           cudaStream_t stream, std::string& err) {
     if (batch <= 0) return 0;
+    // The complete-tree, multi-output and deep-tree kernels keep their key
+    // tables in shared memory and need no device scratch at all.
+    if (f.heap.depth > 0) return launch_heap(f, dtype, x, batch, out, stream, err) ? 0 : 7;
+    if (f.sparse.teams > 0) return launch_sparse(f, dtype, x, batch, out, stream, err) ? 0 : 7;
+    if (f.deep.nodes) return launch_deep(f, dtype, x, batch, out, stream, err) ? 0 : 7;
     const ForestArgs& a = f.args;
     const size_t table = static_cast<size_t>(a.slots) * 32 * sizeof(int);
     if (table > kNoAllocScratchBytes) {

@@ -39,14 +39,19 @@ def noalloc(model, x_ptr: int, batch: int, out_ptr: int) -> int:
 
 def case(i: int):
     rng = np.random.default_rng(77 + i)
-    if i == 0:  # wide: key tables past shared memory, the kernel the path is a variant of
+    if i == 0:  # wide: key tables past shared memory, the generic kernel on the static array
         return random_model(rng, features=1200, trees=300, max_depth=10), edge_inputs(rng, 700, 1200, 0.3)
-    if i == 1:  # the benchmark recipe, small
+    if i == 1:  # the benchmark recipe, small: the complete-tree kernel
         return synth.model_c2(trees=96).to_bytes(), synth.inputs_c2(batch=5000)
-    return random_model(rng, features=7, trees=150, outputs=12, link="softmax"), edge_inputs(rng, 999, 7)
+    if i == 2:  # 12 outputs: the generic kernel
+        return random_model(rng, features=7, trees=150, outputs=12, link="softmax"), edge_inputs(rng, 999, 7)
+    if i == 3:  # 5 classes: the multi-output kernel
+        return synth.model_c4(rounds=20).to_bytes(), synth.inputs_c4(batch=3000)
+    # one output, depth 14: the deep-tree kernel
+    return random_model(rng, features=6, trees=100, max_depth=14), edge_inputs(rng, 2000, 6, 0.3)
 
 
-@pytest.mark.parametrize("i", range(3))
+@pytest.mark.parametrize("i", range(5))
 def test_matches_predict_device_on_two_calls(gpu, i):
     torch = pytest.importorskip("torch")
     model_bytes, x = case(i)
