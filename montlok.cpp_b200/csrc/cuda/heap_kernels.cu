@@ -45,6 +45,7 @@
 #include <mutex>
 #include <vector>
 
+#include "async_copy.cuh"
 #include "device_common.cuh"
 #include "forest.cuh"
 
@@ -55,7 +56,6 @@ constexpr int kTeams = 4;                              // teams of R threads, on
 constexpr int kTrees = 4;                              // trees per chunk = trees one thread walks side by side
 constexpr int kChunksPerBlock = kTreeBlock / kTrees;   // 16
 constexpr int kTileBytes = kPrepTileBytes;            // one warp's transpose tile in the prepare
-constexpr long long kSpinLimit = 1ll << 26;            // mbarrier polls before giving up
 constexpr int kHeapSmemLimit = 227 * 1024;
 constexpr int kMaxSlotBits = 10;
 static_assert(kTreeBlock % kTrees == 0, "chunks never straddle a block of 64 trees");
@@ -64,13 +64,10 @@ __host__ __device__ constexpr int record_bytes(int depth, bool leaf32) {
     return ((4 << depth) + (1 << depth) * (leaf32 ? 4 : 8) + 15) & ~15;
 }
 
-__host__ __device__ constexpr int align128(int n) { return (n + 127) & ~127; }
-
 // Shared memory layout (byte offsets): header (mbarriers [team][2] at 0,
 // buffer-done counters [team][2] at 64, fills issued [team][2] at 96, abort
-// flag at 128) | keys
-// [slots][R] int32 | block partials [2][team][R] double | first buffers of
-// the four teams | second buffers of the four teams. During the prepare the
+// flag at 128) | keys [slots][R] int32 | block partials [2][team][R] double |
+// first buffers of the four teams | second buffers of the four teams. During the prepare the
 // second buffers (not yet refilled) hold the warps' transpose tiles.
 struct Layout {
     int keys, parts, ring0, ring1, total;
@@ -86,70 +83,6 @@ __host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, i
     const int tiles = kTeams * (rows / 32) * kTileBytes;
     l.total = l.ring1 + align128(max(kTeams * chunk, tiles));
     return l;
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Arms `bar` for `bytes` and starts the copy global -> shared (one thread).
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-// Waits for phase `parity` of `bar` to complete; false after kSpinLimit polls
-// or as soon as `*abort` (when given) is raised.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr) {
-    for (long long i = 0; i < kSpinLimit; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if (abort && *abort) return false;
-    }
-    return false;
-}
-
-__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ int lds_s32(uint32_t a) {
-    int v;
-    asm volatile("ld.shared.s32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ double lds_leaf(uint32_t a, bool f32) {
-    if (f32) {
-        float v;
-        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
-        return static_cast<double>(v);
-    }
-    double v;
-    asm volatile("ld.shared.f64 %0, [%1];" : "=d"(v) : "r"(a));
-    return v;
-}
-
-// Starts pulling [p, p + bytes) into L2 (16-byte aligned interior only).
-__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
-    const uintptr_t lo = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t{15};
-    const uintptr_t hi = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t{15};
-    for (uintptr_t a = lo; a < hi; a += (1u << 20)) {
-        const uint32_t n = static_cast<uint32_t>(min(static_cast<uintptr_t>(1u << 20), hi - a));
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
-    }
 }
 
 // One tree walked exactly for one row: the packed compare where the high
