@@ -235,6 +235,28 @@ def test_concurrent_callers_get_the_same_bits(gpu):
     assert same_bits(np.stack(got), expected)
 
 
+def test_concurrent_mixed_calls_on_several_models(gpu):
+    """Threads interleave calls of many shapes on several models (each thread
+    its own workspace and graph cache, evicting shapes past its capacity):
+    every result is the oracle's."""
+    rng = np.random.default_rng(16)
+    models = [synth.model_c2(trees=70).to_bytes(), synth.model_c4(rounds=6).to_bytes(),
+              random_model(rng, features=6, trees=90, max_depth=13)]
+    loaded = [montlok.load(b) for b in models]
+    oracles = [Oracle(b) for b in models]
+    inputs = [synth.inputs_c2(batch=3000), synth.inputs_c4(batch=3000), edge_inputs(rng, 3000, 6)]
+    sizes = [1, 3, 8, 33, 64, 65, 200, 1000, 3000, 7, 2, 129]
+
+    def job(i: int) -> bool:
+        k = i % 3
+        n = sizes[i % len(sizes)]
+        x = inputs[k][(i * 37) % 100:][:n]
+        return same_bits(loaded[k].predict(x).reshape(len(x), -1), oracles[k].predict(x))
+
+    with ThreadPoolExecutor(8) as pool:
+        assert all(pool.map(job, range(96)))
+
+
 def test_stream_is_stateless_predict(gpu):
     rng = np.random.default_rng(8)
     m = montlok.load(random_model(rng, features=4, trees=20))
