@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerates the golden fixtures in this directory from the reference.
 
-Needs the montlok.cpp sources (MONTLOK_REFERENCE, default /root/reference)
-and the reference library compiled from them (``make -C oracle ref``); it is
+Needs the montlok.cpp sources (their directory in MONTLOK_REFERENCE) and
+the reference library compiled from them (``make -C oracle ref``); it is
 run by hand in the development container, never on the GPU box, and its
 outputs are committed:
 
