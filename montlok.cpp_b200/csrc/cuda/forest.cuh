@@ -81,9 +81,14 @@ struct DevForest {
 
 // Queues one predict (out != nullptr) or leaf-index (leaves != nullptr) pass
 // over device buffers on `stream`. `scratch` holds scratch_bytes(f, batch) bytes of
-// device memory (nullptr when that is 0). Returns false with `err` set.
+// device memory (nullptr when that is 0). `counters`, when given, is a buffer
+// of at least kLatencyCounters ints that is zero and that only these
+// launches use (they leave it zero); without it the small-batch kernel's
+// counters live in `scratch` and are cleared on the stream first. Returns
+// false with `err` set.
+inline constexpr int kLatencyCounters = 2;
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
-                   cudaStream_t stream, std::string& err, int* scratch);
+                   cudaStream_t stream, std::string& err, int* scratch, int* counters = nullptr);
 
 // Device scratch a launch of `batch` rows needs: key tables in global memory
 // when a warp's table exceeds shared memory (models with thousands of
@@ -107,7 +112,7 @@ int heap_slot_bits(int slots);
 size_t latency_scratch_bytes(const DevForest& f);
 bool latency_fits(const DevForest& f, long long batch);
 bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
-                    std::string& err, void* scratch);
+                    std::string& err, void* scratch, int* counters);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
 

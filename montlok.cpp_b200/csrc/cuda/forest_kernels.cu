@@ -249,12 +249,12 @@ size_t scratch_bytes(const DevForest& f, long long batch) {
 }
 
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
-                   cudaStream_t stream, std::string& err, int* scratch) {
+                   cudaStream_t stream, std::string& err, int* scratch, int* counters) {
     if (batch <= 0) return true;
     if (out && !leaves && f.heap.depth > 0) {
         if (scratch && latency_fits(f, batch)) {
             return launch_latency(f, dtype, x, batch, out, stream, err,
-                                  reinterpret_cast<unsigned char*>(scratch) + key_scratch_bytes(f));
+                                  reinterpret_cast<unsigned char*>(scratch) + key_scratch_bytes(f), counters);
         }
         return launch_heap(f, dtype, x, batch, out, stream, err);
     }

@@ -345,8 +345,8 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
 // base score) into `bpart` ([block][kLatencyRows]). The last CTA of the row
 // group to finish (a device-scope counter, no waiting) adds the block sums
 // in block order and applies the link: the reference's association
-// (trees.cpp:303-388). `count` ([row groups]) is zeroed on the stream before
-// each launch.
+// (trees.cpp:303-388). `count` ([row groups]) starts at zero and the last CTA
+// of each group sets it back to zero.
 // ---------------------------------------------------------------------------
 constexpr int kLatencyRows = 64;
 constexpr int kLatencyStride = 33;                  // key table row stride (32 rows + 1)
@@ -450,7 +450,10 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
         __threadfence();
     }
     __syncthreads();
-    if (tid == 0) *flag = atomicAdd(&count[group], 1) == blocks - 1;
+    if (tid == 0) {
+        *flag = atomicAdd(&count[group], 1) == blocks - 1;
+        if (*flag) count[group] = 0;  // every CTA of the group has counted: ready for the next launch
+    }
     __syncthreads();
     if (!*flag || tid >= 32 || row >= batch) return;
     // Last CTA of the row group: the block sums in order, then mean and link.
@@ -617,7 +620,7 @@ bool latency_fits(const DevForest& f, long long batch) {
 }
 
 bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
-                    std::string& err, void* scratch) {
+                    std::string& err, void* scratch, int* counters) {
     const HeapArgs& h = f.heap;
     void* k = pick_latency(h.depth, h.leaf32, dtype == 2);
     if (!k) {
@@ -641,8 +644,10 @@ bool launch_latency(const DevForest& f, int dtype, const void* x, long long batc
     const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
     const int groups = static_cast<int>((batch + 31) / 32);
     double* bpart = static_cast<double*>(scratch);
-    int* count = reinterpret_cast<int*>(bpart + static_cast<size_t>(blocks) * kLatencyRows);
-    cudaError_t e = cudaMemsetAsync(count, 0, 2 * sizeof(int), stream);
+    // The kernel leaves its counters at zero: a dedicated zeroed buffer needs
+    // no clearing, counters in the shared scratch do.
+    int* count = counters ? counters : reinterpret_cast<int*>(bpart + static_cast<size_t>(blocks) * kLatencyRows);
+    cudaError_t e = counters ? cudaSuccess : cudaMemsetAsync(count, 0, kLatencyCounters * sizeof(int), stream);
     if (e != cudaSuccess) {
         err = std::string("cudaMemsetAsync: ") + cudaGetErrorString(e);
         return false;

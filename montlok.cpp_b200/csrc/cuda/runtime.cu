@@ -120,6 +120,8 @@ void host_copy(void* dst, const void* src, size_t bytes) {
 }
 
 // A device buffer that only grows.
+// A device buffer that only grows; zeroed when (re)allocated, which the
+// small-batch kernel's self-resetting counters rely on.
 struct DeviceBuffer {
     void* p = nullptr;
     size_t cap = 0;
@@ -128,7 +130,7 @@ struct DeviceBuffer {
         if (p) cudaFree(p);
         p = nullptr;
         cap = 0;
-        if (!device_alloc(&p, bytes, err)) return false;
+        if (!device_alloc(&p, bytes, err) || !ok(cudaMemset(p, 0, bytes), "cudaMemset", err)) return false;
         cap = bytes;
         return true;
     }
@@ -172,6 +174,7 @@ struct CachedGraph {
 struct Workspace {
     cudaStream_t stream[2] = {nullptr, nullptr};
     DeviceBuffer dx[2], dout[2], scratch;
+    DeviceBuffer counters;  // the small-batch kernel's counters: zero between launches, nothing else uses them
     PinnedBuffer hx[2], hout[2];
     std::vector<CachedGraph> graphs;
     unsigned long long tick = 0;
@@ -224,7 +227,8 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
     const size_t in_bytes = batch * static_cast<size_t>(f.args.F) * (dtype == 1 ? 4 : 8);
     const size_t out_bytes = batch * static_cast<size_t>(f.args.K) * sizeof(double);
     const size_t scratch = scratch_bytes(f, static_cast<long long>(batch));
-    if (!w->dx[0].reserve(in_bytes, e) || !w->hx[0].reserve(in_bytes, e) ||
+    if (!w->counters.reserve(kLatencyCounters * sizeof(int), e) || !w->dx[0].reserve(in_bytes, e) ||
+        !w->hx[0].reserve(in_bytes, e) ||
         !w->hout[0].reserve(out_bytes, e) || (scratch && !w->scratch.reserve(scratch, e))) {
         put_error(err, errlen, e);
         return kInternal;
@@ -249,7 +253,7 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
             // buffer (host memory the device addresses directly).
             good = good && launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
                                          static_cast<double*>(w->hout[0].p), nullptr, st, e,
-                                         static_cast<int*>(w->scratch.p));
+                                         static_cast<int*>(w->scratch.p), static_cast<int*>(w->counters.p));
             cudaGraph_t graph = nullptr;
             const cudaError_t end = cudaStreamEndCapture(st, &graph);
             if (good) good = ok(end, "cudaStreamEndCapture", e);
@@ -362,7 +366,7 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     const size_t tail = batch % chunk;
     const size_t scratch = std::max(scratch_bytes(f, static_cast<long long>(chunk)),
                                     tail ? scratch_bytes(f, static_cast<long long>(tail)) : size_t{0});
-    if (scratch && !w->scratch.reserve(scratch, e)) {
+    if ((scratch && !w->scratch.reserve(scratch, e)) || !w->counters.reserve(kLatencyCounters * sizeof(int), e)) {
         put_error(err, errlen, e);
         return kInternal;
     }
@@ -413,7 +417,8 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
             break;
         }
         good = launch_forest(f, dtype, dsrc, static_cast<long long>(rows), leaves ? nullptr : static_cast<double*>(dst_dev),
-                             leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, static_cast<int*>(w->scratch.p));
+                             leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, static_cast<int*>(w->scratch.p),
+                             static_cast<int*>(w->counters.p));
         if (!good) break;
         if (!dev_out) {
             if (pin_out) {

@@ -180,6 +180,21 @@ def test_small_calls_from_pinned_and_pageable_inputs(gpu):
         assert same_bits(m.predict(xs[0]).reshape(rows, 1), o.predict(xs[0]))
 
 
+def test_small_calls_after_a_model_that_dirties_the_scratch(gpu):
+    """A thread's workspace scratch is shared by the models it runs: a wide
+    model's global key tables fill it, then small calls on a complete-tree
+    model (whose kernel counts finished CTAs) must still be exact."""
+    rng = np.random.default_rng(21)
+    wide = random_model(rng, features=1200, trees=40, max_depth=10)
+    xw = edge_inputs(rng, 4000, 1200, 0.3)
+    small = synth.model_c5(trees=200).to_bytes()
+    m_wide, m_small, o_small = montlok.load(wide), montlok.load(small), Oracle(small)
+    for rows in (1, 64, 33, 1):
+        m_wide.predict(xw)
+        x = synth.inputs_c5(batch=rows)
+        assert same_bits(m_small.predict(x).reshape(rows, 1), o_small.predict(x))
+
+
 def test_single_row_and_empty_batch(gpu):
     rng = np.random.default_rng(2)
     model = random_model(rng, features=5, trees=30)
