@@ -63,13 +63,18 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def capture_of(config: str) -> dict:
+    """The committed ncu capture summary of the config's kernel (empty when
+    there is none)."""
+    path = ROOT / "profiles" / f"{config}_dram_traffic.json"
+    return json.loads(path.read_text()) if path.exists() else {}
+
+
 def traffic_per_launch(config: str, rows: int) -> float | None:
     """DRAM bytes of one launch over `rows` rows, from the committed ncu
     capture of the same kernel (bytes per row times rows)."""
-    path = ROOT / "profiles" / f"{config}_dram_traffic.json"
-    if not path.exists():
-        return None
-    return float(json.loads(path.read_text())["dram_bytes_per_row"]) * rows
+    capture = capture_of(config)
+    return float(capture["dram_bytes_per_row"]) * rows if "dram_bytes_per_row" in capture else None
 
 
 class Clocks:
@@ -401,7 +406,8 @@ def main() -> None:
                     "timing": "host clock around the blocking montlok_model_predict call, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
-                         "algorithmic_bytes_per_launch": bytes_per_launch},
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "issue_active_pct_ncu": capture_of(args.config).get("issue_active_pct")},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clock,
         }
