@@ -1,26 +1,27 @@
 // Deep-tree predict kernel for sm_100a: one output, trees too deep for the
 // complete-tree layout (random forests grown to depth 20: c3).
 //
-// Nodes. Every tree is laid out breadth-first with the two children of a
-// split adjacent, 8 bytes a node {W, index of the left child} in one global
-// array; a split's word packs the threshold key and the slot as in the
-// complete-tree kernel, W = (T & ~mask) | slot, and a leaf is
-// {(leaf + 1) << slot_bits | pad slot, own index}: the pad slot's key is
-// INT32_MIN, so a leaf never goes right and the walk stays on it, and its
-// word names the leaf's value in a separate array. A 20-level forest of 9M
-// nodes is 73 MB of nodes plus its leaf values, which stays in the 126 MB L2;
-// node loads carry an evict-last cache policy and the rows an evict-first one
-// so the streaming input does not push the trees out.
+// Records. A tree is cut into two-level records, laid out breadth first: a
+// split, the split words of its two children and the four exits below them,
+// {W top, W left, W right, 0, LL, LR, RL, RR}, 32 bytes that one 256-bit load
+// brings in, so a walk pays one dependent L2 round trip per two levels. Split
+// words pack the threshold key and the slot as in the complete-tree kernel,
+// W = (T & ~mask) | slot; a child that is a leaf gets the pad slot's word
+// (its key is INT32_MIN, so it never goes right) and both its exits name the
+// leaf. An exit is the index of the next record, or, with the top bit set,
+// the number of a leaf value. c3's 200 trees of depth <= 20 are about 80 MB
+// of records and 40 MB of float64 leaf values, held in the 126 MB L2; record
+// loads carry an evict-last cache policy so the streaming input does not push
+// the records out.
 //
 // Work split. Each warp owns 32 rows (a lane per row) and their key tables
 // in shared memory ([slot][32] int32, k | mask for finite keys), independent
 // of the other warps of its CTA. A lane walks kIlp trees side by side, for
-// as many steps as the deepest of them plus one load that reads the leaf it
-// stands on; trees whose walk met a tie in the packed compare are walked
-// again with those splits decided exactly (exact_right). Leaves are added in
-// tree order into 64-tree block partials, block 0 onto the base score, the
-// later blocks added in order: the reference's association
-// (trees.cpp:366-388).
+// as many records as the longest walk among them, then loads the leaf values;
+// trees whose walk met a tie in the packed compare are walked again with
+// those splits decided exactly (exact_right). Leaves are added in tree order
+// into 64-tree block partials, block 0 onto the base score, the later blocks
+// added in order: the reference's association (trees.cpp:366-388).
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -34,7 +35,12 @@ namespace {
 
 constexpr int kIlp = 8;    // trees a lane walks side by side
 constexpr int kWarps = 4;  // warps per CTA, each on its own rows
+// Resident CTAs per SM the register budget is cut for (128 registers a
+// thread): 16 warps with 8 record loads each in flight ran c3 faster than 12
+// warps with 10 or 12, or 20 warps with 6.
+constexpr int kMinCtas = 4;
 constexpr int kSmemLimit = 227 * 1024;
+constexpr uint32_t kLeaf = 0x80000000u;  // exit bit: the rest is a leaf number
 
 __host__ __device__ inline int warp_bytes(int slots) { return slots * 32 * 4 + kPrepTileBytes; }
 
@@ -44,35 +50,56 @@ __device__ __forceinline__ uint64_t evict_last_policy() {
     return p;
 }
 
-__device__ __forceinline__ uint2 ldg_node(const uint2* p, uint64_t policy) {
-    uint2 v;
-    asm volatile("ld.global.nc.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;"
-                 : "=r"(v.x), "=r"(v.y)
+struct Record {
+    uint32_t w[8];
+};
+
+// One record in a single 256-bit load (records are 32-byte aligned).
+__device__ __forceinline__ Record ldg_record(const uint32_t* p, uint64_t policy) {
+    Record r;
+    asm volatile("ld.global.nc.L2::cache_hint.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8], %9;"
+                 : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]), "=r"(r.w[4]), "=r"(r.w[5]),
+                   "=r"(r.w[6]), "=r"(r.w[7])
                  : "l"(p), "l"(policy));
-    return v;
+    return r;
 }
 
-// One tree walked exactly for one row; returns the leaf's node index.
+// The key a split word reads and whether the packed compare tied.
+__device__ __forceinline__ bool goes_right(const int* col, uint32_t w, uint32_t mask, bool& tie) {
+    const int k = col[(w & mask) * 32];
+    tie |= static_cast<uint32_t>(k ^ static_cast<int>(w)) <= mask;
+    return k > static_cast<int>(w);
+}
+
+// One tree walked exactly for one row; returns the exit naming its leaf.
 template <typename XT>
-__device__ __noinline__ uint32_t walk_exact(const ForestArgs& a, const DeepArgs& d, uint32_t root, int depth,
+__device__ __noinline__ uint32_t walk_exact(const ForestArgs& a, const DeepArgs& d, uint32_t p, int steps,
                                             const int* col, uint32_t mask, const XT* __restrict__ x, long long row,
                                             long long batch) {
-    uint32_t p = root;
-    for (int s = 0; s < depth; ++s) {
-        const uint2 n = __ldg(d.nodes + p);
-        const int k = col[(n.x & mask) * 32];
-        bool right = k > static_cast<int>(n.x);
-        if (static_cast<uint32_t>(k ^ static_cast<int>(n.x)) <= mask) {
-            const int node = __ldg(d.node_ids + p);
+    for (int s = 0; s < steps && !(p & kLeaf); ++s) {
+        const uint4* r = reinterpret_cast<const uint4*>(d.records + static_cast<size_t>(p) * 8);
+        const uint4 lo = __ldg(r), hi = __ldg(r + 1);
+        const int* ids = d.node_ids + static_cast<size_t>(p) * 3;
+        bool tie = false;
+        bool right = goes_right(col, lo.x, mask, tie);
+        if (tie) {
+            const int node = __ldg(ids);
             if (node >= 0) right = exact_right(a, x, row, batch, node);
         }
-        p = n.y + (right ? 1u : 0u);
+        const uint32_t wc = right ? lo.z : lo.y;
+        tie = false;
+        bool below = goes_right(col, wc, mask, tie);
+        if (tie) {
+            const int node = __ldg(ids + (right ? 2 : 1));
+            if (node >= 0) below = exact_right(a, x, row, batch, node);
+        }
+        p = right ? (below ? hi.w : hi.z) : (below ? hi.y : hi.x);
     }
     return p;
 }
 
 template <bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kWarps * 32) deep_kernel(const ForestArgs a, const DeepArgs d,
+__global__ void __launch_bounds__(kWarps * 32, kMinCtas) deep_kernel(const ForestArgs a, const DeepArgs d,
                                                             const XT* __restrict__ x, long long batch,
                                                             double* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -98,27 +125,26 @@ __global__ void __launch_bounds__(kWarps * 32) deep_kernel(const ForestArgs a, c
             for (int t0 = b * kTreeBlock; t0 < end; t0 += kIlp) {
                 const int nt = min(kIlp, end - t0);
                 uint32_t p[kIlp];
-                uint2 n[kIlp];
                 bool tie[kIlp];
-                int depth = 0;
+                int steps = 0;
 #pragma unroll
                 for (int t = 0; t < kIlp; ++t) {
-                    p[t] = t < nt ? static_cast<uint32_t>(__ldg(d.roots + t0 + t)) : 0u;
-                    if (t < nt) depth = max(depth, __ldg(a.depth + t0 + t));
+                    p[t] = t < nt ? __ldg(d.roots + t0 + t) : kLeaf;
+                    if (t < nt) steps = max(steps, __ldg(d.steps + t0 + t));
                     tie[t] = false;
                 }
-                for (int s = 0;; ++s) {
+                for (int s = 0; s < steps; ++s) {
+                    Record r[kIlp];
 #pragma unroll
                     for (int t = 0; t < kIlp; ++t) {
-                        if (t < nt) n[t] = ldg_node(d.nodes + p[t], policy);
+                        if (!(p[t] & kLeaf)) r[t] = ldg_record(d.records + static_cast<size_t>(p[t]) * 8, policy);
                     }
-                    if (s == depth) break;  // the last load read the leaf each lane stands on
 #pragma unroll
                     for (int t = 0; t < kIlp; ++t) {
-                        if (t < nt) {
-                            const int k = col[(n[t].x & mask) * 32];
-                            tie[t] |= static_cast<uint32_t>(k ^ static_cast<int>(n[t].x)) <= mask;
-                            p[t] = n[t].y + (k > static_cast<int>(n[t].x) ? 1u : 0u);
+                        if (!(p[t] & kLeaf)) {
+                            const bool right = goes_right(col, r[t].w[0], mask, tie[t]);
+                            const bool below = goes_right(col, right ? r[t].w[2] : r[t].w[1], mask, tie[t]);
+                            p[t] = right ? (below ? r[t].w[7] : r[t].w[6]) : (below ? r[t].w[5] : r[t].w[4]);
                         }
                     }
                 }
@@ -128,17 +154,13 @@ __global__ void __launch_bounds__(kWarps * 32) deep_kernel(const ForestArgs a, c
                 if (__any_sync(0xffffffffu, any)) {
 #pragma unroll
                     for (int t = 0; t < kIlp; ++t) {
-                        if (tie[t]) {
-                            const uint32_t leaf = walk_exact(a, d, __ldg(d.roots + t0 + t), depth, col, mask, x, row,
-                                                             batch);
-                            n[t] = __ldg(d.nodes + leaf);
-                        }
+                        if (tie[t]) p[t] = walk_exact(a, d, __ldg(d.roots + t0 + t), steps, col, mask, x, row, batch);
                     }
                 }
 #pragma unroll
                 for (int t = 0; t < kIlp; ++t) {
                     if (t < nt) {
-                        const uint32_t leaf = (n[t].x >> d.slot_bits) - 1u;
+                        const uint32_t leaf = p[t] & ~kLeaf;
                         const double v = LEAF32 ? static_cast<double>(__ldg(static_cast<const float*>(d.leaves) + leaf))
                                                 : __ldg(static_cast<const double*>(d.leaves) + leaf);
                         part = __dadd_rn(part, v);

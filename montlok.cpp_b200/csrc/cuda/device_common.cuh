@@ -9,7 +9,6 @@
 
 namespace mlk::cuda {
 
-inline constexpr int kTreeBlock = 64;  // trees per partial sum
 inline constexpr int kMaxOut = 8;      // outputs held in registers per pass
 inline constexpr int kIlp = 4;         // trees one lane walks side by side
 inline constexpr int kStage = 33;      // padded row length of the transpose tile

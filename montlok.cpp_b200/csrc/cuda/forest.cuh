@@ -57,13 +57,16 @@ struct SparseArgs {
 };
 
 // Deep-tree layout (deep_kernels.cu); nodes null when the model has none.
+inline constexpr int kTreeBlock = 64;  // trees per partial sum (the reference sums in 64-tree blocks)
+
 struct DeepArgs {
-    int slot_bits;       // low bits of a split word holding the slot
-    int leaf32;          // leaf values are float32
-    const uint2* nodes;  // breadth-first per tree: {word, index of the left child}
-    const void* leaves;  // leaf values, indexed by the leaf number in a leaf's word
-    const int* roots;    // [T]: node index of each tree's root
-    const int* node_ids; // [nodes]: file node of each split, -1 for leaves
+    int slot_bits;            // low bits of a split word holding the slot
+    int leaf32;               // leaf values are float32
+    const uint32_t* records;  // 8 words per record: {W top, W left, W right, 0, exits LL, LR, RL, RR}
+    const void* leaves;       // leaf values, indexed by an exit with the top bit set
+    const uint32_t* roots;    // [T]: exit to each tree's root
+    const int* steps;         // [T]: records on the longest root-to-leaf walk
+    const int* node_ids;      // [3 * records]: file node of each record's three splits, -1 for none
 };
 
 struct DevForest {

@@ -259,7 +259,7 @@ bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch
         return launch_heap(f, dtype, x, batch, out, stream, err);
     }
     if (out && !leaves && f.sparse.teams > 0) return launch_sparse(f, dtype, x, batch, out, stream, err);
-    if (out && !leaves && f.deep.nodes) return launch_deep(f, dtype, x, batch, out, stream, err);
+    if (out && !leaves && f.deep.records) return launch_deep(f, dtype, x, batch, out, stream, err);
     const ForestArgs& a = f.args;
     const Shape s = shape_of(a);
     const bool ties = !a.cast_f32;
@@ -365,7 +365,7 @@ int launch_forest_noalloc(const DevForest& f, int dtype, const void* x, long lon
     // tables in shared memory and need no device scratch at all.
     if (f.heap.depth > 0) return launch_heap(f, dtype, x, batch, out, stream, err) ? 0 : 7;
     if (f.sparse.teams > 0) return launch_sparse(f, dtype, x, batch, out, stream, err) ? 0 : 7;
-    if (f.deep.nodes) return launch_deep(f, dtype, x, batch, out, stream, err) ? 0 : 7;
+    if (f.deep.records) return launch_deep(f, dtype, x, batch, out, stream, err) ? 0 : 7;
     const ForestArgs& a = f.args;
     const size_t table = static_cast<size_t>(a.slots) * 32 * sizeof(int);
     if (table > kNoAllocScratchBytes) {

@@ -445,46 +445,75 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     return 0;
 }
 
-// Builds and uploads the deep-tree node array of `v` into f.deep (left
-// unset when the leaf numbers do not fit a split word). False only on a CUDA
-// error.
+// Builds and uploads the deep-tree records of `v` into f.deep (left unset
+// when the record or leaf numbers do not fit 31 bits). A record is a split,
+// its two children's split words and the four exits below them, so one
+// 32-byte load decides two levels; a child that is a leaf gets the pad word
+// (never goes right) and both its exits name it. Records are laid out tree by
+// tree in breadth-first order. False only on a CUDA error.
 bool upload_deep(const mlk_forest_view* v, DevForest& f, std::string& e) {
     const int T = v->trees;
     const int slot_bits = heap_slot_bits(v->slots);
     const uint32_t mask = (1u << slot_bits) - 1u;
-    std::vector<uint2> nodes;
-    std::vector<int32_t> ids, roots(static_cast<size_t>(T));
+    const uint32_t pad = static_cast<uint32_t>(v->pad_slot);
+    constexpr uint32_t kLeaf = 0x80000000u;
+    constexpr size_t kMaxRecords = size_t{1} << 26;  // 2 GB; shared subtrees unfolded further use the generic kernel
+    std::vector<uint32_t> words;  // 8 per record
+    std::vector<int32_t> ids;     // 3 per record: file node of the top, left and right split, -1 for none
+    std::vector<int32_t> queue;   // file node at the top of each record
+    std::vector<int32_t> level;   // record steps from the tree's root to each record
+    std::vector<uint32_t> roots(static_cast<size_t>(T));
+    std::vector<int32_t> steps(static_cast<size_t>(T), 0);
     std::vector<double> leaves;
-    bool f32 = true;
-    constexpr size_t kMaxNodes = size_t{1} << 31;
-    for (int t = 0; t < T; ++t) {
-        // Breadth first, children adjacent: position i of the tree at base + i.
-        const size_t base = nodes.size();
-        roots[static_cast<size_t>(t)] = static_cast<int32_t>(base);
-        std::vector<int32_t> order{v->roots[t]};
-        for (size_t i = 0; i < order.size(); ++i) {
-            const int node = order[i];
-            if (v->feature[node] >= 0) {
-                const int32_t* w = &v->node_words[static_cast<size_t>(node) * 4];
-                nodes.push_back(make_uint2((static_cast<uint32_t>(w[0]) & ~mask) | static_cast<uint32_t>(w[1]),
-                                           static_cast<uint32_t>(base + order.size())));
-                ids.push_back(node);
-                order.push_back(w[2]);
-                order.push_back(w[3]);
-            } else {
-                const uint64_t leaf = leaves.size() + 1;
-                if (leaf >= (uint64_t{1} << (31 - slot_bits))) return true;  // leaf numbers overflow the word
-                nodes.push_back(make_uint2((static_cast<uint32_t>(leaf) << slot_bits) |
-                                               static_cast<uint32_t>(v->pad_slot),
-                                           static_cast<uint32_t>(base + i)));
-                ids.push_back(-1);
-                const double value = v->leaf_value[node];
-                leaves.push_back(value);
-                f32 = f32 && static_cast<double>(static_cast<float>(value)) == value;
+    bool f32 = true, fits = true;
+    auto split_word = [&](int node) {
+        const int32_t* w = &v->node_words[static_cast<size_t>(node) * 4];
+        return (static_cast<uint32_t>(w[0]) & ~mask) | static_cast<uint32_t>(w[1]);
+    };
+    // The exit to `node` from a record `depth` steps below the root.
+    auto exit_to = [&](int node, int depth, int32_t& need) -> uint32_t {
+        if (v->feature[node] >= 0) {
+            const size_t r = queue.size();
+            if (r >= kMaxRecords) fits = false;
+            queue.push_back(node);
+            level.push_back(depth);
+            return static_cast<uint32_t>(r);
+        }
+        need = std::max(need, depth);
+        const size_t leaf = leaves.size();
+        if (leaf >= kLeaf) fits = false;
+        const double value = v->leaf_value[node];
+        leaves.push_back(value);
+        f32 = f32 && static_cast<double>(static_cast<float>(value)) == value;
+        return kLeaf | static_cast<uint32_t>(leaf);
+    };
+    for (int t = 0; t < T && fits; ++t) {
+        int32_t& need = steps[static_cast<size_t>(t)];
+        size_t i = queue.size();
+        roots[static_cast<size_t>(t)] = exit_to(v->roots[t], 0, need);
+        for (; i < queue.size() && fits; ++i) {
+            const int a = queue[i];
+            const int depth = level[i] + 1;
+            const int32_t* wa = &v->node_words[static_cast<size_t>(a) * 4];
+            uint32_t rec[8] = {split_word(a), pad, pad, 0u, 0u, 0u, 0u, 0u};
+            int32_t id[3] = {a, -1, -1};
+            for (int side = 0; side < 2; ++side) {
+                const int c = wa[2 + side];
+                if (v->feature[c] >= 0) {
+                    const int32_t* wc = &v->node_words[static_cast<size_t>(c) * 4];
+                    rec[1 + side] = split_word(c);
+                    id[1 + side] = c;
+                    rec[4 + 2 * side] = exit_to(wc[2], depth, need);
+                    rec[5 + 2 * side] = exit_to(wc[3], depth, need);
+                } else {
+                    rec[4 + 2 * side] = rec[5 + 2 * side] = exit_to(c, depth, need);
+                }
             }
-            if (nodes.size() >= kMaxNodes) return true;  // shared subtrees unfolded too far
+            words.insert(words.end(), rec, rec + 8);
+            ids.insert(ids.end(), id, id + 3);
         }
     }
+    if (!fits) return true;
     std::vector<float> leaves32;
     if (f32) leaves32.assign(leaves.begin(), leaves.end());
     const size_t leaf_bytes = f32 ? leaves32.size() * 4 : leaves.size() * 8;
@@ -492,27 +521,32 @@ bool upload_deep(const mlk_forest_view* v, DevForest& f, std::string& e) {
     void* dnodes = nullptr;
     void* dleaves = nullptr;
     void* droots = nullptr;
+    void* dsteps = nullptr;
     void* dids = nullptr;
-    if (!device_alloc(&dnodes, nodes.size() * sizeof(uint2), e) ||
-        !ok(cudaMemcpy(dnodes, nodes.data(), nodes.size() * sizeof(uint2), cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+    const size_t word_bytes = words.size() * 4, id_bytes = ids.size() * 4;
+    if (!device_alloc(&dnodes, std::max<size_t>(word_bytes, 32), e) ||
+        !ok(cudaMemcpy(dnodes, words.data(), word_bytes, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
         !device_alloc(&dleaves, std::max<size_t>(leaf_bytes, 16), e) ||
         !ok(cudaMemcpy(dleaves, leaf_src, leaf_bytes, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
         !device_alloc(&droots, roots.size() * 4, e) ||
         !ok(cudaMemcpy(droots, roots.data(), roots.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
-        !device_alloc(&dids, ids.size() * 4, e) ||
-        !ok(cudaMemcpy(dids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
-        for (void* p : {dnodes, dleaves, droots, dids}) {
+        !device_alloc(&dsteps, steps.size() * 4, e) ||
+        !ok(cudaMemcpy(dsteps, steps.data(), steps.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy", e) ||
+        !device_alloc(&dids, std::max<size_t>(id_bytes, 16), e) ||
+        !ok(cudaMemcpy(dids, ids.data(), id_bytes, cudaMemcpyHostToDevice), "cudaMemcpy", e)) {
+        for (void* p : {dnodes, dleaves, droots, dsteps, dids}) {
             if (p) cudaFree(p);
         }
         return false;
     }
-    for (void* p : {dnodes, dleaves, droots, dids}) f.blocks[f.nblocks++] = p;
+    for (void* p : {dnodes, dleaves, droots, dsteps, dids}) f.blocks[f.nblocks++] = p;
     DeepArgs& d = f.deep;
     d.slot_bits = slot_bits;
     d.leaf32 = f32;
-    d.nodes = static_cast<const uint2*>(dnodes);
+    d.records = static_cast<const uint32_t*>(dnodes);
     d.leaves = dleaves;
-    d.roots = static_cast<const int*>(droots);
+    d.roots = static_cast<const uint32_t*>(droots);
+    d.steps = static_cast<const int*>(dsteps);
     d.node_ids = static_cast<const int*>(dids);
     return true;
 }
