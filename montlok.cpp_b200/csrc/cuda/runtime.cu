@@ -6,18 +6,25 @@
 // while one chunk's kernel runs, the next chunk's input is copied host ->
 // device on the other stream (straight from the caller's memory when it is
 // pinned, else through a pinned staging buffer) and the previous chunk's
-// results come back device -> host. Each calling thread has its own
-// workspace per device, so concurrent calls on one model never share
-// buffers.
+// results come back device -> host. Pageable float64 rows of a model that
+// casts its features to float32 (and has no preprocessing) are rounded to
+// float32 while they are staged, halving the bytes on the bus. Staging runs
+// on a pool of host threads. Each calling thread has its own workspace per
+// device, so concurrent calls on one model never share buffers.
 //
 // MONTLOK_FAULT_INJECT=alloc|copy|launch makes the next device allocation,
 // copy or launch of a call fail as if CUDA had failed; tests use it to check
 // that failures surface as MONTLOK_ERROR_INTERNAL with a message.
 #include <algorithm>
 #include <atomic>
+#include <cfenv>
+#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <map>
+#include <mutex>
 #include <memory>
 #include <string>
 #include <thread>
@@ -34,7 +41,12 @@ constexpr int kInternal = 7;
 constexpr int kInvalid = 1;
 constexpr size_t kChunkBytes = size_t{64} << 20;  // input bytes per pipelined chunk
 
-std::atomic<int> g_copy_threads{1};
+std::atomic<int> g_copy_threads{0};  // 0: every hardware thread
+
+int copy_threads() {
+    const int n = g_copy_threads.load(std::memory_order_relaxed);
+    return std::max(1, n > 0 ? n : static_cast<int>(std::thread::hardware_concurrency()));
+}
 
 void put_error(char* err, size_t errlen, const std::string& message) {
     if (!err || errlen == 0) return;
@@ -96,30 +108,115 @@ bool copy_async(void* dst, const void* src, size_t bytes, cudaMemcpyKind kind, c
     return ok(cudaMemcpyAsync(dst, src, bytes, kind, s), "cudaMemcpyAsync", err);
 }
 
-// memcpy split over the library's worker threads for large blocks.
-void host_copy(void* dst, const void* src, size_t bytes) {
-    const int threads = std::max(1, g_copy_threads.load(std::memory_order_relaxed));
-    constexpr size_t kPerThread = size_t{4} << 20;
-    const size_t parts = std::min<size_t>(static_cast<size_t>(threads), std::max<size_t>(1, bytes / kPerThread));
-    if (parts <= 1) {
-        std::memcpy(dst, src, bytes);
-        return;
+// Host worker threads for staging: a job is split into parts that the pool's
+// threads and the calling thread take one at a time, and the caller returns
+// when every part is done. Several callers (one per device) share the pool;
+// since callers work on their own jobs too, a job finishes even if no worker
+// is free (or, after a fork, none exists). Workers start from the default
+// floating-point environment (round to nearest, no flush to zero).
+class HostPool {
+public:
+    static HostPool& get() {
+        static HostPool* pool = new HostPool();  // never destroyed: workers may be blocked at exit
+        return *pool;
     }
-    std::vector<std::thread> pool;
-    const size_t step = (bytes + parts - 1) / parts;
-    for (size_t i = 1; i < parts; ++i) {
-        const size_t lo = i * step, hi = std::min(bytes, lo + step);
-        if (lo < hi) {
-            pool.emplace_back([=] {
-                std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
-            });
+
+    void run(size_t parts, const std::function<void(size_t)>& fn) {
+        if (parts <= 1) {
+            if (parts == 1) fn(0);
+            return;
+        }
+        auto job = std::make_shared<Job>();
+        job->fn = &fn;
+        job->parts = parts;
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            jobs_.push_back(job);
+        }
+        cv_.notify_all();
+        work(*job);
+        std::unique_lock<std::mutex> lock(mu_);
+        done_cv_.wait(lock, [&] { return job->done.load() == job->parts; });
+    }
+
+private:
+    struct Job {
+        const std::function<void(size_t)>* fn = nullptr;
+        size_t parts = 0;
+        std::atomic<size_t> next{0};
+        std::atomic<size_t> done{0};
+    };
+
+    HostPool() {
+        const unsigned n = std::max(1u, std::thread::hardware_concurrency()) - 1;
+        for (unsigned i = 0; i < std::min(n, 255u); ++i) std::thread([this] { loop(); }).detach();
+    }
+
+    // Takes parts of `job` until none is left.
+    void work(Job& job) {
+        for (size_t i; (i = job.next.fetch_add(1)) < job.parts;) {
+            (*job.fn)(i);
+            if (job.done.fetch_add(1) + 1 == job.parts) {
+                std::lock_guard<std::mutex> lock(mu_);
+                done_cv_.notify_all();
+            }
         }
     }
-    std::memcpy(dst, src, std::min(bytes, step));
-    for (auto& t : pool) t.join();
+
+    void loop() {
+        std::fesetenv(FE_DFL_ENV);
+        for (;;) {
+            std::shared_ptr<Job> job;
+            {
+                std::unique_lock<std::mutex> lock(mu_);
+                cv_.wait(lock, [&] {
+                    while (!jobs_.empty() && jobs_.front()->next.load() >= jobs_.front()->parts) jobs_.pop_front();
+                    return !jobs_.empty();
+                });
+                job = jobs_.front();
+            }
+            work(*job);
+        }
+    }
+
+    std::mutex mu_;
+    std::condition_variable cv_, done_cv_;
+    std::deque<std::shared_ptr<Job>> jobs_;
+};
+
+// Splits [0, n) into at most copy_threads() ranges of at least `grain` and
+// runs fn(lo, hi) on each through the pool.
+void host_parallel(size_t n, size_t grain, const std::function<void(size_t, size_t)>& fn) {
+    const size_t parts = std::min<size_t>(static_cast<size_t>(copy_threads()), std::max<size_t>(1, n / grain));
+    const size_t step = (n + parts - 1) / parts;
+    HostPool::get().run(parts, [&](size_t i) {
+        const size_t lo = i * step, hi = std::min(n, lo + step);
+        if (lo < hi) fn(lo, hi);
+    });
 }
 
-// A device buffer that only grows.
+// memcpy split over the worker threads for large blocks.
+void host_copy(void* dst, const void* src, size_t bytes) {
+    host_parallel(bytes, size_t{4} << 20, [&](size_t lo, size_t hi) {
+        std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo);
+    });
+}
+
+// dst[i] = (float)src[i] for n values, split over the worker threads.
+void host_narrow(float* dst, const double* src, size_t n) {
+    host_parallel(n, size_t{512} << 10, [&](size_t lo, size_t hi) {
+        for (size_t i = lo; i < hi; ++i) dst[i] = static_cast<float>(src[i]);
+    });
+}
+
+// Whether this thread converts double to float as the kernels' cast does:
+// round to nearest even, subnormal results kept (no flush to zero).
+bool narrowing_exact() {
+    volatile double up = 1.0 + 0x3p-25, down = 1.0 + 0x1p-25, tiny = 1e-40;
+    return static_cast<float>(up) == 1.0f + 0x1p-23f && static_cast<float>(down) == 1.0f &&
+           static_cast<float>(tiny) != 0.0f && static_cast<float>(-static_cast<double>(up)) == -(1.0f + 0x1p-23f);
+}
+
 // A device buffer that only grows; zeroed when (re)allocated, which the
 // small-batch kernel's self-resetting counters rely on.
 struct DeviceBuffer {
@@ -361,6 +458,16 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     if constexpr (std::is_same_v<Out, double>) {
         if (!leaves && batch <= kGraphRows && !dev_x && !dev_out) return run_small(f, dtype, x, batch, out, err, errlen);
     }
+    // A model that casts features to float32 and has no preprocessing uses
+    // only the float32 value of each double (trees.cpp:275), so pageable rows
+    // are rounded to float32 while they are staged: the staging writes and
+    // the bytes on the bus halve, and the float-input kernels give the same
+    // bits. Pinned rows go to the device as they are: the bus reads them as
+    // fast as the host threads would convert them.
+    const bool narrow = dtype == 2 && !dev_x && !pin_x && f.args.cast_f32 && !f.args.standardize && !f.args.clip &&
+                        narrowing_exact();
+    const int kernel_dtype = narrow ? 1 : dtype;
+    const size_t row_dev = narrow ? static_cast<size_t>(f.args.F) * 4 : row_in;
 
     // Chunks are `chunk` rows but the last one, which may take another kernel.
     const size_t tail = batch % chunk;
@@ -371,8 +478,8 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
         return kInternal;
     }
     for (int s = 0; s < 2; ++s) {
-        if ((!dev_x && !w->dx[s].reserve(chunk * row_in, e)) || (!dev_out && !w->dout[s].reserve(chunk * row_out, e)) ||
-            (!dev_x && !pin_x && !w->hx[s].reserve(chunk * row_in, e)) ||
+        if ((!dev_x && !w->dx[s].reserve(chunk * row_dev, e)) || (!dev_out && !w->dout[s].reserve(chunk * row_out, e)) ||
+            (!dev_x && !pin_x && !w->hx[s].reserve(chunk * row_dev, e)) ||
             (!dev_out && !pin_out && !w->hout[s].reserve(chunk * row_out, e))) {
             put_error(err, errlen, e);
             return kInternal;
@@ -402,11 +509,14 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
         const char* src = static_cast<const char*>(x) + r0 * row_in;
         const void* dsrc = src;
         if (!dev_x) {
-            if (!pin_x) {
+            if (narrow) {
+                host_narrow(static_cast<float*>(w->hx[s].p), reinterpret_cast<const double*>(src), rows * f.args.F);
+                src = static_cast<const char*>(w->hx[s].p);
+            } else if (!pin_x) {
                 host_copy(w->hx[s].p, src, rows * row_in);
                 src = static_cast<const char*>(w->hx[s].p);
             }
-            good = copy_async(w->dx[s].p, src, rows * row_in, cudaMemcpyHostToDevice, st, e);
+            good = copy_async(w->dx[s].p, src, rows * row_dev, cudaMemcpyHostToDevice, st, e);
             dsrc = w->dx[s].p;
         }
         if (!good) break;
@@ -416,7 +526,7 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
             good = false;
             break;
         }
-        good = launch_forest(f, dtype, dsrc, static_cast<long long>(rows), leaves ? nullptr : static_cast<double*>(dst_dev),
+        good = launch_forest(f, kernel_dtype, dsrc, static_cast<long long>(rows), leaves ? nullptr : static_cast<double*>(dst_dev),
                              leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, static_cast<int*>(w->scratch.p),
                              static_cast<int*>(w->counters.p));
         if (!good) break;

@@ -19,7 +19,7 @@ import numpy as np
 import pytest
 
 import montlok
-from forests import edge_inputs, random_model, same_bits
+from forests import GRID, edge_inputs, random_model, same_bits
 from montlok import export, synth
 from oracle import Oracle
 
@@ -178,6 +178,37 @@ def test_small_calls_from_pinned_and_pageable_inputs(gpu):
             assert same_bits(m.predict(x).reshape(want.shape), want)
             assert same_bits(m.predict(xp.numpy()).reshape(want.shape), want)
         assert same_bits(m.predict(xs[0]).reshape(rows, 1), o.predict(xs[0]))
+
+
+# Doubles whose float32 rounding is subnormal, zero, the largest float or
+# infinite.
+NARROWING = [1e-40, -1e-40, 1e-46, -1e-46, 8e-46, 3.5e38, -3.5e38, 3.4028235677973366e38, 3.4028235e38 * (1 + 1e-9)]
+
+
+@pytest.mark.parametrize("decision", ["le", "lt"])
+def test_float32_cast_models_narrow_host_rows(gpu, decision):
+    """Pageable host batches above the small-call size of float32-cast models
+    without preprocessing are rounded to float32 while they are staged.
+    Doubles just beside the thresholds, subnormal, overflowing and infinite
+    values, on complete, deep and shallow forests, must give the reference's
+    bits, as must the same rows from a pinned buffer (sent as float64) and a
+    model with preprocessing (which keeps float64 rows)."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(len(decision) * 7)
+    pre = {"mean": rng.normal(size=6), "scale": rng.uniform(0.5, 2.0, 6), "clip": (-1.2, 1.7)}
+    for depth, trees, preprocess in ((8, 70, None), (14, 90, None), (5, 40, None), (8, 50, pre)):
+        model = random_model(rng, features=6, trees=trees, max_depth=depth, cast="f32", decision=decision,
+                             inf_thresholds=0.05, preprocess=preprocess)
+        x = edge_inputs(rng, 9000, 6, special=0.3)
+        near = rng.random(x.shape) < 0.1
+        scale = rng.choice([-1.0, 1.0], size=int(near.sum())) * 10.0 ** rng.uniform(-15, -6, size=int(near.sum()))
+        x[near] = rng.choice(GRID, size=int(near.sum())) * (1 + scale) + scale
+        odd = rng.random(x.shape) < 0.05
+        x[odd] = rng.choice(np.array(NARROWING), size=int(odd.sum()))
+        check(model, x, leaves=preprocess is None)
+        want = Oracle(model).predict(x)
+        got = montlok.load(model).predict(torch.from_numpy(x).pin_memory().numpy())
+        assert same_bits(got.reshape(want.shape), want)
 
 
 def test_small_calls_after_a_model_that_dirties_the_scratch(gpu):
