@@ -281,6 +281,29 @@ def test_concurrent_callers_get_the_same_bits(gpu):
     assert same_bits(np.stack(got), expected)
 
 
+def test_concurrent_large_host_calls_share_the_staging_pool(gpu):
+    """Threads predict batches of several 64 MB chunks from pageable and
+    pinned host buffers at once, on a float32-cast model (pageable rows
+    narrowed while staged) and a float64 one: the staging jobs share one
+    pool of host threads, and every result equals the same call made alone
+    (and the oracle on a slice)."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(41)
+    models = [synth.model_c2(trees=40).to_bytes(),
+              random_model(rng, features=128, trees=60, max_depth=10, cast="f64")]
+    x = synth.inputs_c2(batch=150_000)
+    pinned = torch.from_numpy(x).pin_memory().numpy()
+    for model in models:
+        m = montlok.load(model)
+        alone = m.predict(x)
+        want = Oracle(model).predict(x[:2000])
+        assert same_bits(alone[:2000].reshape(want.shape), want)
+        with ThreadPoolExecutor(4) as pool:
+            got = list(pool.map(lambda i: m.predict(x if i % 2 == 0 else pinned), range(8)))
+        for g in got:
+            assert same_bits(g, alone)
+
+
 def test_concurrent_mixed_calls_on_several_models(gpu):
     """Threads interleave calls of many shapes on several models (each thread
     its own workspace and graph cache, evicting shapes past its capacity):
