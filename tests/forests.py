@@ -10,6 +10,9 @@ from montlok import export
 
 GRID = np.array([-1.5, -0.25, 0.0, 0.5, 2.0])
 SPECIALS = [np.nan, 0.0, -0.0, 1e-35, -1e-36, 1e-36, np.inf, -np.inf, 1e-300, -1e-300, *GRID]
+# Doubles whose float32 rounding is subnormal, zero, the largest float or
+# infinite.
+NARROWING = [1e-40, -1e-40, 1e-46, -1e-46, 8e-46, 3.5e38, -3.5e38, 3.4028235677973366e38, 3.4028235e38 * (1 + 1e-9)]
 
 
 def random_model(rng: np.random.Generator, features: int = 5, decision: str = "le", cast: str = "f64",

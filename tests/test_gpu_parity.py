@@ -19,7 +19,7 @@ import numpy as np
 import pytest
 
 import montlok
-from forests import GRID, edge_inputs, random_model, same_bits
+from forests import GRID, NARROWING, edge_inputs, random_model, same_bits
 from montlok import export, synth
 from oracle import Oracle
 
@@ -178,11 +178,6 @@ def test_small_calls_from_pinned_and_pageable_inputs(gpu):
             assert same_bits(m.predict(x).reshape(want.shape), want)
             assert same_bits(m.predict(xp.numpy()).reshape(want.shape), want)
         assert same_bits(m.predict(xs[0]).reshape(rows, 1), o.predict(xs[0]))
-
-
-# Doubles whose float32 rounding is subnormal, zero, the largest float or
-# infinite.
-NARROWING = [1e-40, -1e-40, 1e-46, -1e-46, 8e-46, 3.5e38, -3.5e38, 3.4028235677973366e38, 3.4028235e38 * (1 + 1e-9)]
 
 
 @pytest.mark.parametrize("decision", ["le", "lt"])

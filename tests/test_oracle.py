@@ -18,7 +18,7 @@ import numpy as np
 import pytest
 
 import oracle
-from forests import edge_inputs, random_model, same_bits
+from forests import GRID, NARROWING, edge_inputs, random_model, same_bits
 from montlok import export, synth
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -150,6 +150,30 @@ def test_random_ensembles_against_reference(seed):
     o = oracle.Oracle(model)
     assert same_bits(o.predict(x), ref.predict(model, x))
     np.testing.assert_array_equal(o.leaves(x), ref.leaves(model, x))
+
+
+@needs_reference
+@pytest.mark.parametrize("decision, outputs", [("le", 1), ("lt", 1), ("le", 3)])
+def test_float32_cast_models_see_only_the_float32_value(decision, outputs):
+    """The library rounds pageable float64 rows of float32-cast models
+    without preprocessing to float32 on the host. That rests on this
+    property of the reference: such a model gives the same bits for float64
+    rows as for those rows rounded to float32, threshold neighbours,
+    subnormal, overflowing and infinite values included."""
+    rng = np.random.default_rng([len(decision), outputs])
+    model = random_model(rng, features=6, trees=120, max_depth=10, cast="f32", decision=decision, outputs=outputs,
+                         link="softmax" if outputs > 1 else "sigmoid", inf_thresholds=0.05)
+    x = edge_inputs(rng, 3000, 6, special=0.3)
+    near = rng.random(x.shape) < 0.15
+    scale = rng.choice([-1.0, 1.0], size=int(near.sum())) * 10.0 ** rng.uniform(-15, -6, size=int(near.sum()))
+    x[near] = rng.choice(GRID, size=int(near.sum())) * (1 + scale) + scale
+    odd = rng.random(x.shape) < 0.05
+    x[odd] = rng.choice(np.array(NARROWING), size=int(odd.sum()))
+    with np.errstate(over="ignore"):
+        rounded = x.astype(np.float32).astype(np.float64)
+    ref = oracle.Reference()
+    assert same_bits(ref.predict(model, x), ref.predict(model, rounded))
+    np.testing.assert_array_equal(ref.leaves(model, x), ref.leaves(model, rounded))
 
 
 @needs_reference
