@@ -15,12 +15,20 @@ line:
   e2e        rows/s through montlok_model_predict with pinned host buffers:
              host->device input, kernel, device->host output every step
   roofline   the predict kernel's HBM rate on its input bytes (rows x F x 8)
-             against the measured copy bandwidth (MEASURED_PEAKS.json)
+             against the measured copy bandwidth (MEASURED_PEAKS.json), with
+             the DRAM traffic, issue and shared-memory utilisation of the
+             committed ncu capture of the same kernel (profiles/)
   cpu_baseline  the reference runtime (oracle/_ref, compiled from its sources)
              on this host's cores, on a bounded sample of the same workload
+  configs    (one GPU, default c2 run) the same figures for c1, c3 and c4 at
+             their configured batches, and c5's per-call latency
+  sharded    (rank 0) one host-buffer call of the same batch split over all N
+             GPUs by the library itself (montlok_set_devices), strong scaling
 
 ``--impl reference`` times the reference's CPU implementation alone, with all
-host threads, on the same workload and prints the same line.
+host threads, on the same workload (the full batch every step) and prints the
+same line. It imports only the pure-Python model builders of the package and
+the reference library: libmontlok.so is not loaded in that process.
 
 ``--config c5`` is the latency configuration: calls of 1, 8 and 64 rows
 back to back through montlok_model_predict (host buffers; the library
@@ -38,6 +46,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -50,6 +59,7 @@ import numpy as np  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "rows/s (500-tree depth-8 GBDT, 1M rows)"  # BASELINE.json's metric, quoted on c2
+LATENCY_SIZES = (1, 8, 64)
 
 
 def metric_of(cfg) -> str:
@@ -70,15 +80,9 @@ def capture_of(config: str) -> dict:
     return json.loads(path.read_text()) if path.exists() else {}
 
 
-def traffic_per_launch(config: str, rows: int) -> float | None:
-    """DRAM bytes of one launch over `rows` rows, from the committed ncu
-    capture of the same kernel (bytes per row times rows)."""
-    capture = capture_of(config)
-    return float(capture["dram_bytes_per_row"]) * rows if "dram_bytes_per_row" in capture else None
-
-
 class Clocks:
-    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+    """nvidia-smi samples of the SM clock and throttle reasons while running
+    (written to a temporary file)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -86,10 +90,8 @@ class Clocks:
 
     def __init__(self, device: int) -> None:
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_rank{device}.csv"
+        self.out = tempfile.TemporaryFile(mode="w+")
         try:
-            self.path.parent.mkdir(exist_ok=True)
-            self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(device)], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
@@ -101,8 +103,9 @@ class Clocks:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         self.proc.wait()
+        self.out.seek(0)
+        rows = [line.split(", ") for line in self.out.read().splitlines() if line.count(",") >= 8]
         self.out.close()
-        rows = [line.split(", ") for line in self.path.read_text().splitlines() if line.count(",") >= 8]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows]
@@ -122,7 +125,12 @@ def outputs_of(model: bytes) -> int:
     return int(export.read(model)[0]["outputs"]["size"])
 
 
-def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int) -> tuple[float, str, str]:
+# ---------------------------------------------------------------------------
+# CPU side: the reference runtime (or the oracle port without it)
+# ---------------------------------------------------------------------------
+
+
+def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int) -> dict:
     """rows/s of the reference CPU runtime (or the oracle port when the
     reference library is absent) on a bounded sample of `x`."""
     import oracle
@@ -133,7 +141,7 @@ def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int
         ref.set_threads(threads)
         h = ref.open(model)
         try:
-            probe = x[:8192]
+            probe = np.ascontiguousarray(x[:8192])
             out = np.empty((len(probe), K))
             t0 = time.perf_counter()
             ref.predict_handle(h, probe, out)
@@ -146,78 +154,27 @@ def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int
             elapsed = time.perf_counter() - t0
         finally:
             ref.close(h)
-        return rows / elapsed, "reference", f"{rows} rows of the same workload, one montlok_model_predict call"
-    o = oracle.Oracle(model)
-    probe = x[:2048]
-    t0 = time.perf_counter()
-    o.predict(probe, threads=threads)
-    rate = len(probe) / max(time.perf_counter() - t0, 1e-9)
-    rows = int(min(len(x), max(2048, rate * seconds)))
-    t0 = time.perf_counter()
-    o.predict(x[:rows], threads=threads)
-    return rows / (time.perf_counter() - t0), "port", f"{rows} rows of the same workload through the C port"
-
-
-def run_reference(args, cfg, model: bytes, x: np.ndarray) -> dict:
-    """The reference CPU runtime alone, each step a bounded sample of the workload."""
-    import oracle
-
-    threads = os.cpu_count() or 1
-    rows = min(len(x), args.reference_rows)
-    sample = np.ascontiguousarray(x[:rows])
-    out = np.empty((rows, outputs_of(model)))
-    kind = "reference" if oracle.available_reference() else "port"
-    if kind == "reference":
-        ref = oracle.Reference()
-        ref.set_threads(threads)
-        h = ref.open(model)
-        step = lambda: ref.predict_handle(h, sample, out)  # noqa: E731
+        kind, what = "reference", f"{rows} rows of the same workload, one montlok_model_predict call"
     else:
         o = oracle.Oracle(model)
-        step = lambda: o.predict(sample, threads=threads)  # noqa: E731
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    elapsed = time.perf_counter() - t0
-    value = rows * args.steps / elapsed
-    return {"metric": metric_of(cfg), "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": workload(cfg, args),
-            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
-                             "sample": f"{rows} rows of the workload per step"},
-            "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        probe = x[:2048]
+        t0 = time.perf_counter()
+        o.predict(probe, threads=threads)
+        rate = len(probe) / max(time.perf_counter() - t0, 1e-9)
+        rows = int(min(len(x), max(2048, rate * seconds)))
+        t0 = time.perf_counter()
+        o.predict(x[:rows], threads=threads)
+        elapsed = time.perf_counter() - t0
+        kind, what = "port", f"{rows} rows of the same workload through the C port"
+    return {"value": rows / elapsed, "unit": "rows/s", "cores": threads, "kind": kind, "sample": what}
 
 
-LATENCY_SIZES = (1, 8, 64)
-
-
-def latency_stats(samples_ns: np.ndarray) -> dict:
-    return {"p50_us": float(np.percentile(samples_ns, 50)) / 1e3, "p99_us": float(np.percentile(samples_ns, 99)) / 1e3,
-            "mean_us": float(np.mean(samples_ns)) / 1e3, "calls": int(len(samples_ns))}
-
-
-def latency_line(args, cfg, stats: dict, impl: str | None) -> dict:
-    p50 = stats["64"]["p50_us"]
-    line = {"metric": f"p50 us per 64-row call ({cfg.name}: {cfg.describe})", "value": p50, "unit": "us",
-            "n_gpus": args.gpus, "steps": args.calls, "warmup": args.warmup, "ms_per_step": p50 / 1e3,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"{cfg.name}: {cfg.describe}", "call_rows": list(LATENCY_SIZES),
-                       "timing": "per call, inside the library, host buffers in and out"},
-            "latency": stats}
-    if impl:
-        line["impl"] = impl
-    return line
-
-
-def reference_latency(args, model: bytes, x: np.ndarray, threads: int) -> tuple[dict, str]:
-    """Per-call latency of the reference runtime (or None without it)."""
+def reference_latency(calls: int, seconds: float, model: bytes, x: np.ndarray, threads: int) -> dict:
+    """Per-call latency of the reference runtime ({} without it)."""
     import oracle
 
     if not oracle.available_reference():
-        return {}, "unavailable"
+        return {}
     ref = oracle.Reference()
     ref.set_threads(threads)
     h = ref.open(model)
@@ -225,49 +182,214 @@ def reference_latency(args, model: bytes, x: np.ndarray, threads: int) -> tuple[
     try:
         for n in LATENCY_SIZES:
             rows = x[: len(x) // n * n].reshape(-1, n * x.shape[1])
-            calls = max(50, min(args.calls, int(args.cpu_seconds / len(LATENCY_SIZES) * 1e6 / (40.0 * n))))
-            stats[str(n)] = latency_stats(ref.time_calls(h, rows, n, calls, max(10, calls // 10)))
+            count = max(50, min(calls, int(seconds / len(LATENCY_SIZES) * 1e6 / (40.0 * n))))
+            stats[str(n)] = latency_stats(ref.time_calls(h, rows, n, count, max(10, count // 10)))
     finally:
         ref.close(h)
-    return stats, "reference"
+    return stats
 
 
-def run_latency(args, cfg) -> None:
-    """The small-batch configuration on rank 0's GPU (other ranks idle)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+def latency_stats(samples_ns: np.ndarray) -> dict:
+    return {"p50_us": float(np.percentile(samples_ns, 50)) / 1e3, "p99_us": float(np.percentile(samples_ns, 99)) / 1e3,
+            "mean_us": float(np.mean(samples_ns)) / 1e3, "calls": int(len(samples_ns))}
+
+
+def run_reference(args, cfg) -> None:
+    """The reference CPU runtime alone on rank 0, each step the full batch."""
+    import oracle
+    from montlok import synth  # noqa: F401  (pure Python: the model builders)
+
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    model_bytes = cfg.model().to_bytes()
-    x = cfg.inputs(batch=64 * 256)
     threads = os.cpu_count() or 1
-    if args.impl == "reference":
-        stats, kind = reference_latency(args, model_bytes, x, threads)
+    model = cfg.model().to_bytes()
+    if cfg.name == "c5":
+        stats = reference_latency(args.calls, args.cpu_seconds, model, cfg.inputs(batch=64 * 256), threads)
         if not stats:
             print(json.dumps({"impl": "reference", "unavailable": "reference library not built"}), flush=True)
             return
-        line = latency_line(args, cfg, stats, "reference")
-        line["cpu_baseline"] = {"value": stats["64"]["p50_us"], "unit": "us", "cores": threads, "kind": kind,
+        line = latency_line(args, cfg, stats)
+        line["impl"] = "reference"
+        line["cpu_baseline"] = {"value": stats["64"]["p50_us"], "unit": "us", "cores": threads, "kind": "reference",
                                 "sample": "per-call latency, calls of 1, 8 and 64 rows"}
         line["e2e"] = {"value": stats["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
         print(json.dumps(line), flush=True)
         return
-    import torch
+    batch = args.rows or cfg.batch
+    x = cfg.inputs(batch=batch)
+    out = np.empty((batch, outputs_of(model)))
+    kind = "reference" if oracle.available_reference() else "port"
+    if kind == "reference":
+        ref = oracle.Reference()
+        ref.set_threads(threads)
+        h = ref.open(model)
+        step = lambda: ref.predict_handle(h, x, out)  # noqa: E731
+    else:
+        o = oracle.Oracle(model)
+        step = lambda: o.predict(x, threads=threads)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - t0
+    value = batch * args.steps / elapsed
+    line = {"metric": metric_of(cfg), "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": workload(cfg, args, batch),
+            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
+                             "sample": f"the full {batch}-row batch per step, one montlok_model_predict call"},
+            "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    loaded = [p for p in open("/proc/self/maps").read().split() if p.endswith("libmontlok.so")]
+    line["libmontlok_loaded"] = bool(loaded)
+    print(json.dumps(line), flush=True)
 
-    import montlok
 
-    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+
+def workload(cfg, args, batch: int) -> dict:
+    return {"workload": f"{cfg.name}: {cfg.describe}", "rows_per_rank": batch,
+            "l2": "inputs larger than L2 (no flush needed)" if batch * 8 * 32 > 126e6 else
+                  "inputs smaller than L2: a 256 MB buffer is written between timed steps",
+            "parallelism": f"rows sharded, {args.gpus} GPU(s)"}
+
+
+class Measure:
+    """The device-resident and end-to-end timing of one configuration on this
+    rank's GPU."""
+
+    def __init__(self, torch, montlok, model_bytes: bytes, x: np.ndarray, stream) -> None:
+        self.torch, self.montlok = torch, montlok
+        self.model = montlok.load(model_bytes)
+        self.x = x
+        self.batch = len(x)
+        self.K, self.F = self.model.outputs, self.model.features
+        self.stream = stream
+        self.x_dev = torch.from_numpy(x).cuda()
+        self.out_dev = torch.empty((self.batch, self.K), dtype=torch.float64, device="cuda")
+        self.small = self.batch * self.F * 8 < 256 << 20
+        # Writing this buffer between steps evicts the inputs from L2 when they would fit it.
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if self.small else None
+        self.kernel = self.model.kernel(self.batch)
+
+    def step(self) -> None:
+        self.model.predict_device(self.x_dev.data_ptr(), self.batch, self.out_dev.data_ptr(),
+                                  self.montlok._core.FLOAT64, self.stream.cuda_stream)
+
+    def device_ms(self, steps: int, warmup: int, barrier) -> float:
+        torch = self.torch
+        for _ in range(warmup):
+            self.step()
+        barrier()
+        if not self.small:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(self.stream)
+            for _ in range(steps):
+                self.step()
+            end.record(self.stream)
+            barrier()
+            return start.elapsed_time(end) / steps
+        # Inputs that fit L2: flush it before each step, time each step alone.
+        total = 0.0
+        for _ in range(steps):
+            with torch.cuda.stream(self.stream):
+                self.flush.fill_(1)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(self.stream)
+            self.step()
+            end.record(self.stream)
+            end.synchronize()
+            total += start.elapsed_time(end)
+        barrier()
+        return total / steps
+
+    def e2e_ms(self, steps: int, barrier) -> tuple[float, np.ndarray]:
+        torch = self.torch
+        x_pin = torch.from_numpy(self.x).pin_memory()
+        out_pin = torch.empty((self.batch, self.K), dtype=torch.float64).pin_memory()
+        x_np, out_np = x_pin.numpy(), out_pin.numpy()
+        self.model.predict(x_np, out=out_np)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            self.model.predict(x_np, out=out_np)
+        barrier()
+        return (time.perf_counter() - t0) * 1e3 / steps, out_np.copy()
+
+    def check(self, host: np.ndarray) -> None:
+        y_dev = self.out_dev.cpu().numpy()
+        if not np.array_equal(host.view(np.int64), y_dev.view(np.int64)):
+            raise SystemExit("host-buffer and device-buffer predictions differ")
+
+    def launches_per_step(self) -> int:
+        K = self.K
+        if self.kernel in ("generic", "generic-global-keys"):
+            return (K + 7) // 8 + (1 if (K > 8 and self.model.spec["config"].get("link") == "softmax") else 0)
+        return 1
+
+
+def roofline(config: str, ms: float, batch: int, F: int) -> dict:
+    peak, peak_kind = peaks()
+    bytes_per_launch = batch * F * 8
+    achieved = bytes_per_launch / (ms / 1e3) / 1e9
+    capture = capture_of(config)
+    per_row = capture.get("dram_bytes_per_row")
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": f"{peak_kind} hbm_gbs", "traffic": float(per_row) * batch if per_row else None,
+            "algorithmic_bytes_per_launch": bytes_per_launch,
+            "ncu_capture": {k: capture.get(k) for k in ("kernel", "captured_rows", "issue_active_pct",
+                                                         "smem_pipe_pct", "warp_inst_per_warp_tree") if k in capture}}
+
+
+def config_figures(torch, montlok, cfg, args, barrier, batch: int, cpu: bool) -> dict:
+    """Device rows/s, e2e rows/s, roofline and CPU baseline of one config on this GPU."""
+    model_bytes = cfg.model().to_bytes()
+    x = cfg.inputs(batch=batch)
+    m = Measure(torch, montlok, model_bytes, x, torch.cuda.Stream())
+    ms = m.device_ms(args.steps, args.warmup, barrier)
+    e2e_ms, host = m.e2e_ms(args.e2e_steps, barrier)
+    m.check(host)
+    fig = {"metric": metric_of(cfg), "kernel": m.kernel, "rows": batch, "value": batch / (ms / 1e3),
+           "unit": "rows/s", "ms_per_step": ms,
+           "e2e": {"value": batch / (e2e_ms / 1e3), "unit": "rows/s", "ms_per_step": e2e_ms,
+                   "h2d_bytes_per_step": batch * m.F * 8, "d2h_bytes_per_step": batch * m.K * 8},
+           "roofline": roofline(cfg.name, ms, batch, m.F), "gpu_launches": args.steps * m.launches_per_step()}
+    if cpu:
+        fig["cpu_baseline"] = cpu_reference_rate(model_bytes, x, args.cpu_seconds, os.cpu_count() or 1)
+    del m
+    torch.cuda.empty_cache()
+    return fig
+
+
+def latency_line(args, cfg, stats: dict) -> dict:
+    p50 = stats["64"]["p50_us"]
+    return {"metric": f"p50 us per 64-row call ({cfg.name}: {cfg.describe})", "value": p50, "unit": "us",
+            "n_gpus": args.gpus, "steps": args.calls, "warmup": args.warmup, "ms_per_step": p50 / 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: {cfg.describe}", "call_rows": list(LATENCY_SIZES),
+                       "timing": "per call, inside the library, host buffers in and out"},
+            "latency": stats}
+
+
+def latency_figures(torch, montlok, cfg, args, cpu: bool) -> dict:
+    """c5: per-call latency of 1, 8 and 64-row host-buffer calls, the device
+    time of a 64-row launch, and the reference's per-call latency."""
+    model_bytes = cfg.model().to_bytes()
     model = montlok.load(model_bytes)
-    clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    x = cfg.inputs(batch=64 * 256)
     stats = {}
     for n in LATENCY_SIZES:
         rows = x[: len(x) // n * n].reshape(-1, n * model.features)
         samples, _ = montlok._core.bench(model, rows, batch=n, iterations=args.calls)
         stats[str(n)] = latency_stats(samples)
-    # Device time of one 64-row predict (inputs resident), CUDA events.
     xd = torch.from_numpy(np.ascontiguousarray(x[:64])).cuda()
     od = torch.empty((64, model.outputs), dtype=torch.float64, device="cuda")
     stream = torch.cuda.Stream()
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, 3)):
         model.predict_device(xd.data_ptr(), 64, od.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
@@ -275,24 +397,61 @@ def run_latency(args, cfg) -> None:
         model.predict_device(xd.data_ptr(), 64, od.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
     end.record(stream)
     torch.cuda.synchronize()
-    line = latency_line(args, cfg, stats, None)
-    line["device_us_per_64_rows"] = start.elapsed_time(end) * 10.0
-    line["e2e"] = {"value": stats["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 64 * model.features * 8,
-                   "d2h_bytes_per_step": 64 * model.outputs * 8}
+    fig = {"latency": stats, "kernel": {str(n): model.kernel(n) for n in LATENCY_SIZES},
+           "device_us_per_64_rows": start.elapsed_time(end) * 10.0,
+           "gpu_launches": args.calls * len(LATENCY_SIZES)}
+    if cpu:
+        threads = os.cpu_count() or 1
+        ref = reference_latency(args.calls, args.cpu_seconds, model_bytes, x, threads)
+        if ref:
+            fig["cpu_baseline"] = {"value": ref["64"]["p50_us"], "unit": "us", "cores": threads, "kind": "reference",
+                                   "sample": "per-call latency, calls of 1, 8 and 64 rows", "latency": ref}
+    return fig
+
+
+def run_latency(args, cfg) -> None:
+    """The small-batch configuration on rank 0's GPU (other ranks idle)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+
+    import montlok
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    fig = latency_figures(torch, montlok, cfg, args, cpu=not args.no_cpu)
+    line = latency_line(args, cfg, fig["latency"])
+    line["device_us_per_64_rows"] = fig["device_us_per_64_rows"]
+    line["kernel"] = fig["kernel"]
+    line["e2e"] = {"value": fig["latency"]["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 64 * 200 * 8,
+                   "d2h_bytes_per_step": 64 * 8}
     line["roofline"] = None
-    line["gpu_launches"] = args.calls * len(LATENCY_SIZES)
+    line["gpu_launches"] = fig["gpu_launches"]
     line["clocks"] = clocks.stop()
-    if not args.no_cpu:
-        ref_stats, kind = reference_latency(args, model_bytes, x, threads)
-        if ref_stats:
-            line["cpu_baseline"] = {"value": ref_stats["64"]["p50_us"], "unit": "us", "cores": threads, "kind": kind,
-                                    "sample": "per-call latency, calls of 1, 8 and 64 rows", "latency": ref_stats}
+    if "cpu_baseline" in fig:
+        line["cpu_baseline"] = fig["cpu_baseline"]
     print(json.dumps(line), flush=True)
 
 
-def workload(cfg, args) -> dict:
-    return {"workload": f"{cfg.name}: {cfg.describe}", "rows_per_rank": args.rows or cfg.batch,
-            "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"rows sharded, {args.gpus} GPU(s)"}
+def sharded_call(torch, montlok, cfg, world: int, batch: int, steps: int) -> dict:
+    """One host-buffer call of `batch` pinned rows that the library splits
+    over devices 0..world-1 itself (montlok_set_devices), timed on the host
+    around the blocking call: strong scaling of a single call."""
+    model = montlok.load(cfg.model().to_bytes())
+    x_pin = torch.from_numpy(cfg.inputs(batch=batch)).pin_memory()
+    out_pin = torch.empty((batch, model.outputs), dtype=torch.float64).pin_memory()
+    x_np, out_np = x_pin.numpy(), out_pin.numpy()
+    montlok.set_devices(world)
+    try:
+        model.predict(x_np, out=out_np)  # uploads to every device, first-touch of the workers
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            model.predict(x_np, out=out_np)
+        ms = (time.perf_counter() - t0) * 1e3 / steps
+    finally:
+        montlok.set_devices(0)
+    return {"devices": world, "rows": batch, "value": batch / (ms / 1e3), "unit": "rows/s", "ms_per_call": ms,
+            "h2d_bytes_per_call": batch * model.features * 8, "timing": "host clock around one blocking call"}
 
 
 def main() -> None:
@@ -305,8 +464,9 @@ def main() -> None:
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--e2e-steps", type=int, default=3)
     parser.add_argument("--cpu-seconds", type=float, default=8.0)
-    parser.add_argument("--reference-rows", type=int, default=65536)
     parser.add_argument("--no-cpu", action="store_true")
+    parser.add_argument("--configs", default="c1,c3,c4,c5",
+                        help="other configurations measured on one GPU beside the default c2 line ('' for none)")
     parser.add_argument("--calls", type=int, default=20000, help="timed calls per size (latency configuration)")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -314,6 +474,9 @@ def main() -> None:
     from montlok import synth
 
     cfg = synth.CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
     if args.config == "c5":
         run_latency(args, cfg)
         return
@@ -321,14 +484,6 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     batch = args.rows or cfg.batch
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        model = cfg.model().to_bytes()
-        x = cfg.inputs(batch=min(batch, max(args.reference_rows, 8192)))
-        print(json.dumps(run_reference(args, cfg, model, x)), flush=True)
-        return
 
     import torch
     import torch.distributed as dist
@@ -347,74 +502,55 @@ def main() -> None:
         torch.cuda.synchronize()
 
     model_bytes = cfg.model().to_bytes()
-    model = montlok.load(model_bytes)
     x = cfg.inputs(batch=batch)
-    K, F = model.outputs, model.features
-    x_dev = torch.from_numpy(x).cuda()
-    out_dev = torch.empty((batch, K), dtype=torch.float64, device="cuda")
-    stream = torch.cuda.Stream()
-    launches_per_step = (K + 7) // 8 + (1 if (K > 8 and model.spec["config"].get("link") == "softmax") else 0)
-
-    def step():
-        model.predict_device(x_dev.data_ptr(), batch, out_dev.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
-
+    m = Measure(torch, montlok, model_bytes, x, torch.cuda.Stream())
     clocks = Clocks(local)
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    end.record(stream)
-    barrier()
-    ms = start.elapsed_time(end) / args.steps
-    y_dev = out_dev.cpu().numpy()
-
-    # End to end through the reference-facing call: pinned host buffers, copies inside.
-    x_pin = torch.from_numpy(x).pin_memory()
-    out_pin = torch.empty((batch, K), dtype=torch.float64).pin_memory()
-    out_np = out_pin.numpy()
-    x_np = x_pin.numpy()
-    model.predict(x_np, out=out_np)
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        model.predict(x_np, out=out_np)
-    barrier()
-    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+    ms = m.device_ms(args.steps, args.warmup, barrier)
+    e2e_ms, host = m.e2e_ms(args.e2e_steps, barrier)
     clock = clocks.stop()
-    if not np.array_equal(out_np.view(np.int64), y_dev.view(np.int64)):
-        raise SystemExit("host-buffer and device-buffer predictions differ")
+    m.check(host)
 
     from montlok.distributed import max_over_ranks
 
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], device="cuda")
 
+    line = None
     if rank == 0:
-        peak, peak_kind = peaks()
-        bytes_per_launch = batch * F * 8
-        achieved = bytes_per_launch / (ms / 1e3) / 1e9
-        traffic = traffic_per_launch(args.config, batch)
         line = {
             "metric": metric_of(cfg), "value": world * batch / (ms / 1e3), "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": workload(cfg, args),
-            "e2e": {"value": world * batch / (e2e_ms / 1e3), "unit": "rows/s", "h2d_bytes_per_step": batch * F * 8,
-                    "d2h_bytes_per_step": batch * K * 8, "ms_per_step": e2e_ms,
+            "config": workload(cfg, args, batch), "kernel": m.kernel,
+            "e2e": {"value": world * batch / (e2e_ms / 1e3), "unit": "rows/s", "h2d_bytes_per_step": batch * m.F * 8,
+                    "d2h_bytes_per_step": batch * m.K * 8, "ms_per_step": e2e_ms,
                     "timing": "host clock around the blocking montlok_model_predict call, max over ranks"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
-                         "algorithmic_bytes_per_launch": bytes_per_launch,
-                         "issue_active_pct_ncu": capture_of(args.config).get("issue_active_pct")},
-            "gpu_launches": args.steps * launches_per_step,
+            "roofline": roofline(args.config, ms, batch, m.F),
+            "gpu_launches": args.steps * m.launches_per_step(),
             "clocks": clock,
         }
+    del m, x
+    torch.cuda.empty_cache()
+    # Strong scaling of one call split by the library over every rank's GPU:
+    # rank 0 alone, while the other ranks wait at the barrier.
+    if world > 1 or args.gpus > 1:
+        if rank == 0:
+            line["sharded"] = sharded_call(torch, montlok, cfg, max(world, args.gpus), batch, args.e2e_steps)
+        if world > 1:
+            dist.barrier()
+    if rank == 0:
         if world == 1 and not args.no_cpu:
-            rate, kind, sample = cpu_reference_rate(model_bytes, x, args.cpu_seconds, os.cpu_count() or 1)
-            line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": os.cpu_count() or 1, "kind": kind,
-                                    "sample": sample}
+            line["cpu_baseline"] = cpu_reference_rate(model_bytes, cfg.inputs(batch=batch), args.cpu_seconds,
+                                                      os.cpu_count() or 1)
+        if world == 1 and args.config == "c2" and args.configs:
+            configs = {}
+            for name in [n for n in args.configs.split(",") if n]:
+                other = synth.CONFIGS[name]
+                if name == "c5":
+                    configs[name] = latency_figures(torch, montlok, other, args, cpu=not args.no_cpu)
+                else:
+                    configs[name] = config_figures(torch, montlok, other, args, barrier, other.batch,
+                                                   cpu=not args.no_cpu)
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

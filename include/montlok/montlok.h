@@ -153,6 +153,20 @@ MONTLOK_API int montlok_model_predict_leaves(const montlok_model* model, montlok
                                              size_t batch, int32_t* leaves);
 MONTLOK_API int montlok_model_predict_leaves_device(const montlok_model* model, montlok_dtype dtype, const void* x,
                                                     size_t batch, int32_t* leaves, void* stream);
+/* Additive. The device-buffer calls (predict_device, predict_leaves_device,
+ * predict_device_noalloc) return before their kernels run, so a kernel that
+ * gives up a bounded wait on its tree data (its rows are then not written)
+ * cannot fail the call itself. This reports it: MONTLOK_ERROR_INTERNAL when
+ * such a kernel on the current device gave up since the last check (the
+ * record is then cleared), else MONTLOK_OK. Call it after synchronising the
+ * streams of those calls. Host-buffer calls report the same failure from the
+ * call itself. */
+MONTLOK_API int montlok_model_device_status(const montlok_model* model);
+/* Additive. The kernel a predict of `batch` rows runs on the current device
+ * (the model is uploaded there first): "complete-tree", "small-batch",
+ * "multi-output", "deep-tree", "generic" or "generic-global-keys". The
+ * string is static. */
+MONTLOK_API int montlok_model_kernel(const montlok_model* model, size_t batch, const char** name);
 /* Additive. Trees of a model (the leaves row length). */
 MONTLOK_API int montlok_model_trees(const montlok_model* model, uint32_t* trees);
 

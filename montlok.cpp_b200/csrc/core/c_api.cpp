@@ -193,6 +193,21 @@ int montlok_model_predict_leaves_device(const montlok_model* model, montlok_dtyp
     });
 }
 
+int montlok_model_device_status(const montlok_model* model) {
+    return guard([&] {
+        require(model != nullptr, "null model");
+        model->impl->check_device_status();
+    });
+}
+
+int montlok_model_kernel(const montlok_model* model, size_t batch, const char** name) {
+    if (name) *name = "";
+    return guard([&] {
+        require(model && name, "null argument");
+        *name = model->impl->kernel_name(batch);
+    });
+}
+
 int montlok_model_trees(const montlok_model* model, uint32_t* trees) {
     return guard([&] {
         require(model && trees, "null argument");

@@ -279,12 +279,6 @@ void Model::predict_device(InputType type, const void* x, size_t batch, double* 
 void Model::predict_device_noalloc(InputType type, const void* x, size_t batch, double* out, void* stream) const {
     if (batch == 0) return;
     check_call(type, x, out);
-    const size_t table = static_cast<size_t>(forest_->slots) * 32 * sizeof(int32_t);
-    if (table > mlk_cuda_noalloc_scratch_bytes()) {
-        fail(Status::Unsupported, "the model needs " + std::to_string(table) + " bytes of key table per 32 rows, more "
-                                  "than the " + std::to_string(mlk_cuda_noalloc_scratch_bytes()) +
-                                  "-byte scratch of the no-allocation path");
-    }
     char err[kErr] = {0};
     int current = 0;
     check_cuda(mlk_cuda_current_device(&current, err, sizeof err), err);
@@ -295,6 +289,26 @@ void Model::predict_device_noalloc(InputType type, const void* x, size_t batch, 
                                 "(those calls allocate), after which the no-allocation entry point can run");
     }
     check_cuda(mlk_cuda_predict_device_noalloc(f, static_cast<int>(type), x, batch, out, stream, err, sizeof err), err);
+}
+
+void Model::check_device_status() const {
+    char err[kErr] = {0};
+    int current = 0;
+    check_cuda(mlk_cuda_current_device(&current, err, sizeof err), err);
+    const mlk_dev_forest* f = devices_->find(current);
+    if (f && mlk_cuda_forest_status(f, 1) != 0) {
+        fail(Status::Internal, "a device-buffer predict on CUDA device " + std::to_string(current) +
+                                   " gave up waiting for its tree data (bounded wait ran out); its rows were not "
+                                   "written");
+    }
+}
+
+const char* Model::kernel_name(size_t batch) const {
+    char err[kErr] = {0};
+    int count = 0, current = 0;
+    check_cuda(mlk_cuda_device_count(&count, err, sizeof err), err);
+    check_cuda(mlk_cuda_current_device(&current, err, sizeof err), err);
+    return mlk_cuda_kernel_name(devices_->on(current), batch);
 }
 
 void Model::predict_leaves(InputType type, const void* x, size_t batch, int32_t* leaves, bool device,

@@ -181,6 +181,12 @@ public:
     // Leaf node index of every (row, tree); host or device buffers.
     void predict_leaves(InputType type, const void* x, size_t batch, int32_t* leaves, bool device,
                         void* stream) const;
+    // Throws Error(Internal) when a device-buffer call on the current device
+    // gave up a bounded wait since the last check, and clears that record.
+    void check_device_status() const;
+    // The kernel a predict of `batch` rows runs on the current device
+    // (uploads the model there first).
+    const char* kernel_name(size_t batch) const;
 
 private:
     explicit Model(std::shared_ptr<const Archive> archive);

@@ -1,7 +1,7 @@
 // Shared-memory streaming helpers of the tree kernels: explicit 32-bit shared
 // addresses and loads, mbarrier-counted one-dimensional bulk async copies
-// (cp.async.bulk, global -> this CTA's shared memory), bounded waits, and L2
-// prefetch of the next rows.
+// (cp.async.bulk, global -> this CTA's shared memory), time-bounded waits, and
+// L2 prefetch of the next rows.
 #pragma once
 
 #include <cstddef>
@@ -9,9 +9,17 @@
 
 namespace mlk::cuda {
 
-inline constexpr long long kSpinLimit = 1ll << 26;  // mbarrier polls before a wait gives up
+// How long a wait on a copy may take before the kernel gives up (ns of the
+// GPU's global timer); kernels receive it as a launch argument.
+inline constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
 __host__ __device__ constexpr int align128(int n) { return (n + 127) & ~127; }
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -31,18 +39,27 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
-// Waits for phase `parity` of `bar` to complete; false after kSpinLimit polls
-// or as soon as `*abort` (when given) is raised.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr) {
-    for (long long i = 0; i < kSpinLimit; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (done) return true;
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete; false once `limit_ns` of the
+// global timer have passed (or after 2^30 polls, whichever comes first), or as
+// soon as `*abort` (when given) is raised.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long limit_ns,
+                                          const volatile int* abort = nullptr) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (int polls = 0; polls < (1 << 30); ++polls) {
+        if (mbar_try(bar, parity)) return true;
         if (abort && *abort) return false;
+        if (global_ns() - t0 > limit_ns) return false;
     }
     return false;
 }

@@ -27,7 +27,13 @@ struct ForestArgs {
     const int* counts;          // [K]
     const double* threshold;    // [nodes]
     const int* feature;         // [nodes]
-    int* status;                // mapped host word: nonzero after a kernel gave up waiting
+    // Per call: the mapped host word a kernel sets to 1 when a wait on its
+    // tree copies runs out (then its rows are not written), how long such a
+    // wait may take, and a fault-injection switch that makes the kernels
+    // issue no tree copy at all, so every wait runs out (tests only).
+    int* status;
+    unsigned long long wait_ns;
+    int skip_copies;
 };
 
 // Complete-tree layout (heap_kernels.cu); depth 0 when the model has none.
@@ -36,7 +42,6 @@ struct HeapArgs {
     int slot_bits;               // low bits of a split word holding the slot
     const unsigned char* trees;  // whole chunks of heap_record_bytes(depth, leaf32) records, inert trees last
     const int* node_ids;         // [T * (2^depth - 1)]: file node of each heap split, -1 for padding
-    int* status;
 };
 
 // Multi-output layout (sparse_kernels.cu); teams 0 when the model has none.

@@ -367,6 +367,9 @@ int launch_forest_noalloc(const DevForest& f, int dtype, const void* x, long lon
     if (f.sparse.teams > 0) return launch_sparse(f, dtype, x, batch, out, stream, err) ? 0 : 7;
     if (f.deep.records) return launch_deep(f, dtype, x, batch, out, stream, err) ? 0 : 7;
     const ForestArgs& a = f.args;
+    // The generic kernel keeps its key tables in shared memory too when they
+    // fit; only wider models use the static array.
+    if (!shape_of(a).global_keys) return launch_forest(f, dtype, x, batch, out, nullptr, stream, err, nullptr) ? 0 : 7;
     const size_t table = static_cast<size_t>(a.slots) * 32 * sizeof(int);
     if (table > kNoAllocScratchBytes) {
         err = "the model needs " + std::to_string(table) + " bytes of key table per 32 rows, more than the " +
@@ -406,6 +409,16 @@ int launch_forest_noalloc(const DevForest& f, int dtype, const void* x, long lon
 
 }  // namespace
 }  // namespace mlk::cuda
+
+extern "C" const char* mlk_cuda_kernel_name(const mlk_dev_forest* forest, size_t batch) {
+    using namespace mlk::cuda;
+    const DevForest& f = forest->f;
+    const long long rows = static_cast<long long>(batch);
+    if (f.heap.depth > 0) return latency_fits(f, rows) ? "small-batch" : "complete-tree";
+    if (f.sparse.teams > 0) return "multi-output";
+    if (f.deep.records) return "deep-tree";
+    return shape_of(f.args).global_keys ? "generic-global-keys" : "generic";
+}
 
 extern "C" size_t mlk_cuda_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 

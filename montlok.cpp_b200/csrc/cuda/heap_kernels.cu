@@ -39,7 +39,7 @@
 // is a full chunk. Waits are bounded: a warp whose wait runs out raises the
 // CTA's abort flag, every wait gives up once the flag is up, the CTA leaves
 // at the next round barrier after waiting (bounded) for its copies in flight,
-// and the forest's status word records the error for the host.
+// and the call's status word records the error for the host.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     // (to wait out copies in flight before an early exit).
     uint32_t consumed[2] = {0u, 0u};
     auto issue = [&](int q) {
+        if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
         const int b = q & 1;
         bulk_load(b ? buf1 : buf0, h.trees + static_cast<size_t>(chunk_at(q)) * kChunkBytes, kChunkBytes,
                   &team_bar[b]);
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
                 for (int c = 0; c < cn; ++c, ++q) {
                     const int b = q & 1;
                     // Warp-uniform: the walk's votes need every lane.
-                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, abort));
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns, abort));
                     ++consumed[b];
                     if (ok) {
                         walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
@@ -309,10 +310,10 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
             // Leave no bulk copy in flight into shared memory: wait (bounded)
             // for the last copy issued to each buffer, then stop.
             if (producer) {
-                if (team == 0) atomicExch(h.status, 1);
+                if (team == 0) atomicExch(a.status, 1);
                 for (int b = 0; b < 2; ++b) {
                     const unsigned n = fills[2 * team + b];
-                    if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u);
+                    if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u, a.wait_ns);
                 }
             }
             return;
@@ -388,7 +389,7 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && !a.skip_copies) {
         bulk_load(smem_u32(trees), h.trees + static_cast<size_t>(t0) * kRec, static_cast<uint32_t>(copied * kRec), bar);
     }
     // Keys of the group's live rows: value i is (row row0 + i / F, feature
@@ -422,12 +423,18 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
     }
     if (tid < 32) keys[a.pad_slot * kLatencyStride + tid] = INT_MIN;
     __syncthreads();
-    if (!__all_sync(0xffffffffu, mbar_wait(bar, 0u))) {
-        if (lane == 0) atomicExch(h.status, 1);
-        return;  // the row group's sum never completes; the host reads the status word
+    const bool arrived = __syncthreads_and(mbar_wait(bar, 0u, a.wait_ns));
+    if (!arrived && tid == 0) {
+        // The block's trees never arrived: record the failure for the host
+        // (this call's results are void) and leave no copy in flight into
+        // shared memory (a second bounded wait for an issued one). The CTA
+        // still counts itself below, so the row group's counter returns to
+        // zero for the next launch.
+        atomicExch(a.status, 1);
+        if (!a.skip_copies) mbar_wait(bar, 0u, a.wait_ns);
     }
     const long long row = row0 + lane;
-    if (warp * kTrees < copied) {
+    if (arrived && warp * kTrees < copied) {
         double v[kTrees];
         walk_leaves<D, kLatencyStride, LEAF32>(a, h, smem_u32(trees) + warp * kTrees * kRec,
                                                smem_u32(keys) + lane * 4, mask, t0 + warp * kTrees, x, row, batch, v);
@@ -435,7 +442,7 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
         for (int t = 0; t < kTrees; ++t) leafv[(warp * kTrees + t) * 32 + lane] = v[t];
     }
     __syncthreads();
-    if (tid < 32 && row < batch) {
+    if (arrived && tid < 32 && row < batch) {
         double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
         for (int t0 = 0; t0 < nt; t0 += 8) {
             double v[8];  // the loads together, the adds in order

@@ -78,6 +78,14 @@ int mlk_cuda_leaves_device(const mlk_dev_forest* forest, int dtype, const void* 
 size_t mlk_cuda_noalloc_scratch_bytes(void);
 int mlk_cuda_predict_device_noalloc(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch,
                                     double* out, void* stream, char* err, size_t errlen);
+/* The status word of the forest's device-buffer calls: nonzero when one of
+ * their kernels gave up a bounded wait on its tree copies since the word was
+ * last cleared (its rows were then not written). `clear` resets it. */
+int mlk_cuda_forest_status(const mlk_dev_forest* forest, int clear);
+/* The kernel a predict of `batch` rows runs on this forest: "complete-tree",
+ * "small-batch", "multi-output", "deep-tree", "generic" or
+ * "generic-global-keys". */
+const char* mlk_cuda_kernel_name(const mlk_dev_forest* forest, size_t batch);
 int mlk_cuda_predict_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
                           char* err, size_t errlen);
 int mlk_cuda_leaves_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,

@@ -15,6 +15,10 @@
 // MONTLOK_FAULT_INJECT=alloc|copy|launch makes the next device allocation,
 // copy or launch of a call fail as if CUDA had failed; tests use it to check
 // that failures surface as MONTLOK_ERROR_INTERNAL with a message.
+// MONTLOK_FAULT_INJECT=wait launches the kernels with their tree copies
+// switched off and a 2 ms wait limit, so every wait on a copy runs out: the
+// kernels give up cleanly (no copy is in flight) and set the call's status
+// word, which the host reports as MONTLOK_ERROR_INTERNAL.
 #include <algorithm>
 #include <atomic>
 #include <cfenv>
@@ -31,6 +35,7 @@
 #include <type_traits>
 #include <vector>
 
+#include "async_copy.cuh"
 #include "forest.cuh"
 #include "mlk_cuda.h"
 
@@ -58,6 +63,20 @@ void put_error(char* err, size_t errlen, const std::string& message) {
 bool injected(const char* what) {
     const char* v = std::getenv("MONTLOK_FAULT_INJECT");
     return v && std::strcmp(v, what) == 0;
+}
+
+constexpr unsigned long long kInjectedWaitNs = 2000000ull;
+
+// The kernel arguments of one call: the forest's, with the call's status
+// word and, under MONTLOK_FAULT_INJECT=wait, no tree copies and a short wait.
+DevForest call_forest(const DevForest& f, int* status, bool fault_wait) {
+    DevForest g = f;
+    g.args.status = status;
+    if (fault_wait) {
+        g.args.skip_copies = 1;
+        g.args.wait_ns = kInjectedWaitNs;
+    }
+    return g;
 }
 
 bool ok(cudaError_t e, const char* what, std::string& err) {
@@ -270,6 +289,11 @@ struct CachedGraph {
 
 struct Workspace {
     cudaStream_t stream[2] = {nullptr, nullptr};
+    // The status word of this thread's host calls (mapped pinned memory): the
+    // kernels set it when a wait on their tree copies runs out; cleared
+    // before every call and read after it.
+    int* status_host = nullptr;
+    int* status_dev = nullptr;
     DeviceBuffer dx[2], dout[2], scratch;
     DeviceBuffer counters;  // the small-batch kernel's counters: zero between launches, nothing else uses them
     PinnedBuffer hx[2], hout[2];
@@ -283,6 +307,7 @@ struct Workspace {
         for (auto s : stream) {
             if (s) cudaStreamDestroy(s);
         }
+        if (status_host) cudaFreeHost(status_host);
     }
 };
 
@@ -293,6 +318,14 @@ Workspace* workspace(int device, std::string& err) {
         auto fresh = std::make_unique<Workspace>();
         for (auto& s : fresh->stream) {
             if (!ok(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate", err)) return nullptr;
+        }
+        void* word = nullptr;
+        if (!ok(cudaHostAlloc(&word, sizeof(int), cudaHostAllocMapped), "cudaHostAlloc", err)) return nullptr;
+        fresh->status_host = static_cast<int*>(word);
+        *fresh->status_host = 0;
+        if (!ok(cudaHostGetDevicePointer(reinterpret_cast<void**>(&fresh->status_dev), word, 0),
+                "cudaHostGetDevicePointer", err)) {
+            return nullptr;
         }
         w = std::move(fresh);
     }
@@ -313,14 +346,18 @@ constexpr size_t kGraphCache = 8;    // graphs kept per workspace
 // forest, input type and row count (or after a staging buffer grew), so
 // later calls of the same shape pay one graph launch instead of separate
 // stream operations and kernel launches.
-int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double* out, char* err, size_t errlen) {
+int run_small(const DevForest& base, int dtype, const void* x, size_t batch, double* out, char* err,
+              size_t errlen) {
     std::string e;
-    DeviceGuard guard(f.device);
-    Workspace* w = workspace(f.device, e);
+    DeviceGuard guard(base.device);
+    Workspace* w = workspace(base.device, e);
     if (!w) {
         put_error(err, errlen, e);
         return kInternal;
     }
+    const bool fault_wait = injected("wait");
+    const DevForest f = call_forest(base, w->status_dev, fault_wait);
+    *reinterpret_cast<volatile int*>(w->status_host) = 0;
     const size_t in_bytes = batch * static_cast<size_t>(f.args.F) * (dtype == 1 ? 4 : 8);
     const size_t out_bytes = batch * static_cast<size_t>(f.args.K) * sizeof(double);
     const size_t scratch = scratch_bytes(f, static_cast<long long>(batch));
@@ -337,6 +374,25 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
         if (c.forest == f.uid && c.dtype == dtype && c.batch == batch && std::equal(buffers, buffers + 5, c.buffers)) {
             g = &c;
         }
+    }
+    if (fault_wait) {
+        // The injected launch is never cached: run it on the stream directly.
+        std::memcpy(w->hx[0].p, x, in_bytes);
+        bool good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e) &&
+                    launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
+                                  static_cast<double*>(w->hout[0].p), nullptr, st, e,
+                                  static_cast<int*>(w->scratch.p), static_cast<int*>(w->counters.p)) &&
+                    ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
+        if (good && *reinterpret_cast<volatile int*>(w->status_host) != 0) {
+            e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
+            good = false;
+        }
+        if (!good) {
+            put_error(err, errlen, e);
+            return kInternal;
+        }
+        std::memcpy(out, w->hout[0].p, out_bytes);
+        return 0;
     }
     if (!g) {
         bool good = ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture", e);
@@ -416,7 +472,7 @@ int run_small(const DevForest& f, int dtype, const void* x, size_t batch, double
     bool good = ok(cudaGraphLaunch(g->exec, st), "cudaGraphLaunch", e) &&
                 ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
     if (good) std::memcpy(out, w->hout[0].p, out_bytes);
-    if (good && f.status_host && *reinterpret_cast<volatile int*>(f.status_host) != 0) {
+    if (good && *reinterpret_cast<volatile int*>(w->status_host) != 0) {
         e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
         good = false;
     }
@@ -435,15 +491,17 @@ struct Pending {
 };
 
 template <typename Out>
-int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* out, size_t out_per_row, bool leaves,
-             char* err, size_t errlen) {
+int run_host(const DevForest& base, int dtype, const void* x, size_t batch, Out* out, size_t out_per_row,
+             bool leaves, char* err, size_t errlen) {
     std::string e;
-    DeviceGuard guard(f.device);
-    Workspace* w = workspace(f.device, e);
+    DeviceGuard guard(base.device);
+    Workspace* w = workspace(base.device, e);
     if (!w) {
         put_error(err, errlen, e);
         return kInternal;
     }
+    const DevForest f = call_forest(base, w->status_dev, injected("wait"));
+    *reinterpret_cast<volatile int*>(w->status_host) = 0;
     const size_t elem = dtype == 1 ? 4 : 8;
     const size_t row_in = static_cast<size_t>(f.args.F) * elem;
     const size_t row_out = out_per_row * sizeof(Out);
@@ -456,7 +514,9 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
     const bool pin_x = kx == MLK_PTR_PINNED, pin_out = ko == MLK_PTR_PINNED;
     const bool dev_x = kx == MLK_PTR_DEVICE, dev_out = ko == MLK_PTR_DEVICE;
     if constexpr (std::is_same_v<Out, double>) {
-        if (!leaves && batch <= kGraphRows && !dev_x && !dev_out) return run_small(f, dtype, x, batch, out, err, errlen);
+        if (!leaves && batch <= kGraphRows && !dev_x && !dev_out) {
+            return run_small(base, dtype, x, batch, out, err, errlen);
+        }
     }
     // A model that casts features to float32 and has no preprocessing uses
     // only the float32 value of each double (trees.cpp:275), so pageable rows
@@ -544,7 +604,7 @@ int run_host(const DevForest& f, int dtype, const void* x, size_t batch, Out* ou
         if (good) good = ok(cudaStreamSynchronize(w->stream[s]), "cudaStreamSynchronize", e);
         else cudaStreamSynchronize(w->stream[s]);
     }
-    if (good && f.status_host && *reinterpret_cast<volatile int*>(f.status_host) != 0) {
+    if (good && *reinterpret_cast<volatile int*>(w->status_host) != 0) {
         e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
         good = false;
     }
@@ -950,8 +1010,9 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     a.counts = reinterpret_cast<const int*>(at(i_counts));
     a.threshold = reinterpret_cast<const double*>(at(i_thr));
     a.feature = reinterpret_cast<const int*>(at(i_feat));
-    // The status word kernels raise when a bounded wait runs out: mapped
-    // pinned memory, so the host reads it without a copy.
+    // The status word of device-buffer calls (host-buffer calls use their
+    // workspace's): mapped pinned memory, so the host reads it without a
+    // copy; montlok_model_device_status reads and clears it.
     void* status = nullptr;
     if (!ok(cudaHostAlloc(&status, sizeof(int), cudaHostAllocMapped), "cudaHostAlloc", e) ||
         !ok(cudaHostGetDevicePointer(reinterpret_cast<void**>(&a.status), status, 0), "cudaHostGetDevicePointer", e)) {
@@ -962,7 +1023,8 @@ int mlk_cuda_forest_upload(int device, const mlk_forest_view* v, mlk_dev_forest*
     }
     f.status_host = static_cast<int*>(status);
     *f.status_host = 0;
-    f.heap.status = a.status;
+    a.wait_ns = kWaitLimitNs;
+    a.skip_copies = 0;
     // Complete-tree records: [2^d split words, the last unused] [2^d leaves],
     // 16-byte aligned; a split word is (T & ~mask) | slot.
     const int D = v->complete_depth;
@@ -1084,8 +1146,8 @@ static int device_call(const mlk_dev_forest* forest, int dtype, const void* x, s
         e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
         good = false;
     } else {
-        good = launch_forest(forest->f, dtype, x, static_cast<long long>(batch), out, leaves, st, e,
-                             static_cast<int*>(tmp));
+        const DevForest f = call_forest(forest->f, forest->f.args.status, injected("wait"));
+        good = launch_forest(f, dtype, x, static_cast<long long>(batch), out, leaves, st, e, static_cast<int*>(tmp));
     }
     if (tmp) cudaFreeAsync(tmp, st);
     if (!good) {
@@ -1110,6 +1172,14 @@ int mlk_cuda_predict_host(const mlk_dev_forest* forest, int dtype, const void* x
     if (batch == 0) return 0;
     return mlk::cuda::run_host<double>(forest->f, dtype, x, batch, out, static_cast<size_t>(forest->f.args.K), false,
                                        err, errlen);
+}
+
+int mlk_cuda_forest_status(const mlk_dev_forest* forest, int clear) {
+    volatile int* word = forest->f.status_host;
+    if (!word) return 0;
+    const int value = *word;
+    if (clear && value) *word = 0;
+    return value;
 }
 
 int mlk_cuda_leaves_host(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, int32_t* leaves,

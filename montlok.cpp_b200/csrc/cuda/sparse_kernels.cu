@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
 
     uint32_t consumed[2] = {0u, 0u};
     auto issue = [&](int q) {
+        if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
         const int b = q & 1;
         bulk_load(b ? buf1 : buf0, stream + static_cast<size_t>(q) * chunk_bytes, static_cast<uint32_t>(chunk_bytes),
                   &team_bar[b]);
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
         int cur = 0;
         for (int q = 0; q < chunks; ++q) {
             const int b = q & 1;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, abort));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns, abort));
             ++consumed[b];
             if (ok) {
                 const uint32_t buf = b ? buf1 : buf0;
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
                 if (team == 0) atomicExch(a.status, 1);
                 for (int b = 0; b < 2; ++b) {
                     const unsigned n = fills[2 * team + b];
-                    if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u);
+                    if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u, a.wait_ns);
                 }
             }
             return;

@@ -23,11 +23,12 @@ import os
 import platform
 from typing import Any
 
-from . import _core
-from ._core import (FormatError, Model, Stream, device_count, devices, families, latency_threads, set_devices,
-                    set_latency_threads, set_threads, threads)
-
-__version__: str = _core.version()
+# The native library loads with the first use of a name that needs it (below),
+# so the pure-Python submodules (export, synth) import without it: the
+# reference benchmark arm and the CPU checkers use them beside the reference
+# runtime without mapping libmontlok.so into their process.
+_CORE_NAMES = ("FormatError", "Model", "Stream", "device_count", "devices", "families", "latency_threads",
+               "set_devices", "set_latency_threads", "set_threads", "threads")
 
 __all__ = ["FormatError", "Model", "Stream", "__version__", "build_info", "device_count", "devices", "export",
            "families", "latency_threads", "load", "load_plugin", "set_devices", "set_latency_threads",
@@ -35,40 +36,50 @@ __all__ = ["FormatError", "Model", "Stream", "__version__", "build_info", "devic
 
 _SUBMODULES = ("export", "synth", "cli")
 
+# The library's montlok_version(); a test checks that the two agree.
+__version__ = "0.2.0"
 
-def load(source: Any) -> Model:
+
+def _native():
+    """montlok._core (raises ImportError when libmontlok.so is missing)."""
+    core = importlib.import_module("._core", __name__)
+    if not hasattr(core.Model, "spec"):
+        core.Model.spec = property(lambda self: json.loads(self.spec_json))
+    return core
+
+
+def load(source: Any):
     """Opens a model from a path, the file's bytes, or a binary file object."""
+    core = _native()
     if isinstance(source, (bytes, bytearray, memoryview)):
-        return Model.from_bytes(bytes(source))
+        return core.Model.from_bytes(bytes(source))
     if hasattr(source, "read"):
-        return Model.from_bytes(source.read())
-    return Model.open(os.fspath(source))
+        return core.Model.from_bytes(source.read())
+    return core.Model.open(os.fspath(source))
 
 
 def load_plugin(path: str | os.PathLike) -> None:
     """Plugin families are CPU code and not part of this build: raises NotImplementedError."""
-    _core.load_plugin(os.fspath(path))
-
-
-def _spec(self: Model) -> dict:
-    return json.loads(self.spec_json)
-
-
-Model.spec = property(_spec)  # type: ignore[attr-defined]
+    _native().load_plugin(os.fspath(path))
 
 
 def build_info() -> dict:
     """Version, ABI, families, thread and GPU settings, for logs and status pages."""
-    return {"version": __version__, "abi": _core.abi_version(), "families": families(), "threads": threads(),
-            "latency_threads": latency_threads(), "devices": devices(), "device_count": device_count(),
-            "machine": platform.machine(), "python": platform.python_version(), "rdt_extension": False}
+    core = _native()
+    return {"version": core.version(), "abi": core.abi_version(), "families": core.families(),
+            "threads": core.threads(), "latency_threads": core.latency_threads(), "devices": core.devices(),
+            "device_count": core.device_count(), "machine": platform.machine(),
+            "python": platform.python_version(), "rdt_extension": False}
 
 
 def __getattr__(name: str) -> Any:
     if name in _SUBMODULES:
         return importlib.import_module(f".{name}", __name__)
+    if name in _CORE_NAMES or name == "_core":
+        core = _native()
+        return core if name == "_core" else getattr(core, name)
     raise AttributeError(f"module 'montlok' has no attribute {name!r}")
 
 
 def __dir__() -> list[str]:
-    return sorted(set(globals()) | set(_SUBMODULES))
+    return sorted(set(globals()) | set(_SUBMODULES) | set(_CORE_NAMES))

@@ -59,6 +59,8 @@ _sig("montlok_model_predict_device", _i32, _vp, _i32, _vp, _sz, _vp, _vp)
 _sig("montlok_model_predict_leaves", _i32, _vp, _i32, _vp, _sz, _vp)
 _sig("montlok_model_predict_leaves_device", _i32, _vp, _i32, _vp, _sz, _vp, _vp)
 _sig("montlok_model_trees", _i32, _vp, ctypes.POINTER(ctypes.c_uint32))
+_sig("montlok_model_device_status", _i32, _vp)
+_sig("montlok_model_kernel", _i32, _vp, _sz, ctypes.POINTER(ctypes.c_char_p))
 _sig("montlok_stream_open", _i32, _vp, _sz, ctypes.POINTER(_vp))
 _sig("montlok_stream_step", _i32, _vp, _i32, _vp, _vp)
 _sig("montlok_stream_reset", _i32, _vp)
@@ -282,6 +284,18 @@ class Model:
     def predict_device(self, x_ptr: int, batch: int, out_ptr: int, dtype: int = FLOAT64, stream: int = 0) -> None:
         """Raw device pointers on the current CUDA device; queued on `stream`."""
         _check(lib.montlok_model_predict_device(self._h, int(dtype), x_ptr, int(batch), out_ptr, stream))
+
+    def check_device_status(self) -> None:
+        """Raises RuntimeError when a device-buffer predict on the current
+        device gave up waiting for its tree data since the last check (its
+        rows were not written); call it after synchronising those calls."""
+        _check(lib.montlok_model_device_status(self._h))
+
+    def kernel(self, batch: int) -> str:
+        """The kernel a predict of `batch` rows runs on the current device."""
+        name = ctypes.c_char_p()
+        _check(lib.montlok_model_kernel(self._h, int(batch), ctypes.byref(name)))
+        return (name.value or b"").decode()
 
     def predict_leaves(self, x: Any) -> np.ndarray:
         """int32 node index of the leaf each row reaches in each tree: [batch, trees]."""

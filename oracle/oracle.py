@@ -28,7 +28,19 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "libmontlok_oracle.so"
 REF_LIB = HERE / "_ref" / "libmontlok_ref.so"
-REFERENCE_SOURCES = Path(os.environ.get("MONTLOK_REFERENCE", "/root/reference"))
+
+
+def reference_sources() -> Path | None:
+    """The reference's source tree: the directory named by MONTLOK_REFERENCE,
+    else a checkout called ``reference`` beside this repository; None when
+    neither holds its sources (then nothing of the reference is built)."""
+    for where in (os.environ.get("MONTLOK_REFERENCE"), HERE.parent.parent / "reference"):
+        if where and (Path(where) / "src" / "core" / "trees.cpp").exists():
+            return Path(where)
+    return None
+
+
+REFERENCE_SOURCES = reference_sources()
 sys.path.insert(0, str(HERE.parent / "montlok.cpp_b200" / "python"))
 
 from montlok import export  # noqa: E402  (the model-file reader)
@@ -39,9 +51,11 @@ _LINKS = {"identity": 0, "sigmoid": 1, "softmax": 2, "exp": 3}
 def build(reference: bool = True) -> None:
     """Builds the oracle (and the reference library when its sources exist)."""
     targets = ["oracle"]
-    if reference and (REFERENCE_SOURCES / "src" / "core" / "trees.cpp").exists():
+    variables = []
+    if reference and REFERENCE_SOURCES is not None:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REFERENCE_SOURCES}", *targets], check=True)
+        variables.append(f"REF={REFERENCE_SOURCES}")
+    subprocess.run(["make", "-s", "-C", str(HERE), *variables, *targets], check=True)
 
 
 class _Forest(ctypes.Structure):

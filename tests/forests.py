@@ -4,6 +4,8 @@ LightGBM's zero band, infinities, thresholds themselves)."""
 
 from __future__ import annotations
 
+import functools
+
 import numpy as np
 
 from montlok import export
@@ -65,3 +67,40 @@ def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
         return False
     nan = np.isnan(a)
     return bool(np.array_equal(nan, np.isnan(b)) and np.array_equal(a[~nan].view(np.int64), b[~nan].view(np.int64)))
+
+
+@functools.lru_cache(maxsize=None)
+def full_model(name: str) -> bytes:
+    """The benchmark recipe `name` at its configured size (built once per process)."""
+    from montlok import synth
+
+    return synth.CONFIGS[name].model().to_bytes()
+
+
+def near_thresholds(model: bytes, x: np.ndarray, rng: np.random.Generator, frac: float = 0.08) -> np.ndarray:
+    """A copy of `x` with a fraction of its values moved onto the split rules of
+    the model's own trees: each picked (row, feature) takes a threshold of a
+    random split on that feature, exactly, one double ulp either side, its
+    float32 rounding, the float32 neighbours of that, or the midpoints between
+    them (doubles that round to the float32 value from above or below)."""
+    spec, t = export.read(model)
+    p = (spec.get("config") or {}).get("tensors", "trees")
+    feature, threshold = t[p + ".feature"], t[p + ".threshold"]
+    split = feature >= 0
+    by_feature: dict[int, np.ndarray] = {}
+    for f in np.unique(feature[split]):
+        values = threshold[split & (feature == f)]
+        by_feature[int(f)] = values[np.isfinite(values)]
+    y = np.array(x, dtype=np.float64, copy=True)
+    rows, cols = np.nonzero(rng.random(y.shape) < frac)
+    for r, c in zip(rows, cols):
+        pool = by_feature.get(int(c))
+        if pool is None or len(pool) == 0:
+            continue
+        th = float(pool[rng.integers(len(pool))])
+        f32 = np.float32(th)
+        up32, down32 = np.nextafter(f32, np.float32(np.inf)), np.nextafter(f32, np.float32(-np.inf))
+        choices = [th, np.nextafter(th, np.inf), np.nextafter(th, -np.inf), float(f32), float(up32), float(down32),
+                   (float(f32) + float(up32)) / 2, (float(f32) + float(down32)) / 2]
+        y[r, c] = choices[int(rng.integers(len(choices)))]
+    return y

@@ -31,12 +31,15 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("MONTLOK_REFERENCE", "/root/reference"))
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "montlok.cpp_b200" / "python"))
 sys.path.insert(0, str(ROOT / "tests"))
 
 import oracle  # noqa: E402
+
+REF = oracle.reference_sources()
+if REF is None:
+    raise SystemExit("the reference sources are needed: set MONTLOK_REFERENCE to their directory")
 from forests import edge_inputs, random_model  # noqa: E402
 from montlok import synth  # noqa: E402
 

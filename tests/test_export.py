@@ -17,17 +17,18 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+import oracle
 from golden.make_golden import lightgbm_dump, xgboost_tree
 from montlok import export, synth
 
-REF = Path(os.environ.get("MONTLOK_REFERENCE", "/root/reference"))
+REF = oracle.reference_sources()
 
 
 @pytest.fixture(scope="module")
 def ref_export():
+    if REF is None:
+        pytest.skip("reference sources absent (set MONTLOK_REFERENCE)")
     path = REF / "python/montlok/export.py"
-    if not path.exists():
-        pytest.skip("reference sources absent")
     spec = importlib.util.spec_from_file_location("montlok_reference_export_t", path)
     module = importlib.util.module_from_spec(spec)
     sys.modules[spec.name] = module
