@@ -268,8 +268,12 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
                 double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
                 for (int c = 0; c < cn; ++c, ++q) {
                     const int b = q & 1;
-                    // Warp-uniform: the walk's votes need every lane.
-                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns, abort));
+                    // Warp-uniform: the walk's votes need every lane. Once the
+                    // CTA is aborting no wait is trusted: a warp whose own wait
+                    // ran out has lost count of the barrier's phases, and a
+                    // wait on the other parity would return at once.
+                    const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u,
+                                                                                 a.wait_ns, abort));
                     ++consumed[b];
                     if (ok) {
                         walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,

@@ -244,7 +244,11 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
         int cur = 0;
         for (int q = 0; q < chunks; ++q) {
             const int b = q & 1;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns, abort));
+            // Once the CTA is aborting no wait is trusted: a warp whose own
+            // wait ran out has lost count of the barrier's phases, and a wait
+            // on the other parity would return at once.
+            const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns,
+                                                                         abort));
             ++consumed[b];
             if (ok) {
                 const uint32_t buf = b ? buf1 : buf0;
