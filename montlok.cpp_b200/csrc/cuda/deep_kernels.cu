@@ -15,7 +15,7 @@
 // the records out.
 //
 // Work split. Each warp owns 32 rows (a lane per row) and their key tables
-// in shared memory ([slot][32] int32, k | mask for finite keys), independent
+// in shared memory ([slot][32] int32, (k & ~mask) | slot), independent
 // of the other warps of its CTA. A lane walks kIlp trees side by side, for
 // as many records as the longest walk among them, then loads the leaf values;
 // trees whose walk met a tie in the packed compare are walked again with
@@ -42,7 +42,7 @@ constexpr int kMinCtas = 4;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint32_t kLeaf = 0x80000000u;  // exit bit: the rest is a leaf number
 
-__host__ __device__ inline int warp_bytes(int slots) { return slots * 32 * 4 + kPrepTileBytes; }
+__host__ __device__ inline int warp_bytes(int slots) { return slots * 32 * 4; }
 
 __device__ __forceinline__ uint64_t evict_last_policy() {
     uint64_t p;
@@ -66,8 +66,8 @@ __device__ __forceinline__ Record ldg_record(const uint32_t* p, uint64_t policy)
 
 // The key a split word reads and whether the packed compare tied.
 __device__ __forceinline__ bool goes_right(const int* col, uint32_t w, uint32_t mask, bool& tie) {
-    const int k = col[(w & mask) * 32];
-    tie |= static_cast<uint32_t>(k ^ static_cast<int>(w)) <= mask;
+    const int k = col[(w & mask) * 32];  // (key & ~mask) | slot: the word's low bits
+    tie |= k == static_cast<int>(w);
     return k > static_cast<int>(w);
 }
 
@@ -105,7 +105,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) deep_kernel(const Fores
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* keys = reinterpret_cast<int*>(smem + warp * warp_bytes(a.slots));
-    double* tile = reinterpret_cast<double*>(smem + warp * warp_bytes(a.slots) + a.slots * 32 * 4);
     const uint32_t mask = (1u << d.slot_bits) - 1u;
     const uint64_t policy = evict_last_policy();
     const long long groups = (batch + 31) / 32;
@@ -115,7 +114,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) deep_kernel(const Fores
     const int* col = keys + lane;
     for (long long g = me; g < groups; g += all) {
         const long long row0 = g * 32, row = row0 + lane;
-        prepare_rows<32>(a, x, row0, batch, keys, tile, lane, 0, a.F, static_cast<int>(mask));
+        __syncwarp();  // the previous group's walks are done with the table
+        prepare_own_row<32>(a, x, row, batch, keys + lane, 0, a.F, static_cast<int>(mask));
         keys[a.pad_slot * 32 + lane] = INT_MIN;
         __syncwarp();
         double acc = 0.0;

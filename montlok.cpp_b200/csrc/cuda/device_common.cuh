@@ -40,17 +40,21 @@ __device__ __forceinline__ double finish(const ForestArgs& a, double v, double m
 }
 
 // Writes the keys of one prepared value into every slot (variant) its
-// feature uses; `low` is ORed into the keys of values that are neither NaN
-// nor in the zero band (the complete-tree kernel keeps only their high bits).
+// feature uses. With a nonzero `mask` (the packed-word kernels, whose split
+// words are (T & ~mask) | slot) every key keeps only its high bits and
+// carries its own slot in the low ones, (key & ~mask) | slot: a key read
+// for a split then has the split word's low bits, so `key > word` compares
+// the high bits alone and `key == word` is exactly a tie of the high bits.
+__device__ __forceinline__ void key_of(const ForestArgs& a, double v, int& k, bool& nan, bool& zero);
 template <int STRIDE>
-__device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, double v, int low = 0) {
-    const bool nan = v != v;
-    const int k = (a.cast_f32 ? key32(__double2float_rn(v)) : key32(__double2float_rd(v))) | low;
-    const bool zero = nan || fabs(v) <= kZeroThr;
-    if (s.x >= 0) col[s.x * STRIDE] = nan ? INT_MAX : k;
-    if (s.y >= 0) col[s.y * STRIDE] = nan ? INT_MIN : k;
-    if (s.z >= 0) col[s.z * STRIDE] = zero ? INT_MAX : k;
-    if (s.w >= 0) col[s.w * STRIDE] = zero ? INT_MIN : k;
+__device__ __forceinline__ void put_made_keys(int* col, int4 s, int k, bool nan, bool zero, int mask);
+
+template <int STRIDE>
+__device__ __forceinline__ void put_keys(const ForestArgs& a, int* col, int4 s, double v, int mask = 0) {
+    int k;
+    bool nan, zero;
+    key_of(a, v, k, nan, zero);
+    put_made_keys<STRIDE>(col, s, k, nan, zero, mask);
 }
 
 // Builds the key table columns of 32 rows starting at row0: the warp reads
@@ -97,6 +101,94 @@ __device__ void prepare_group(const ForestArgs& a, const XT* __restrict__ x, lon
     __syncwarp();
 }
 
+// The key of one prepared value (see put_keys) with its NaN and LightGBM
+// zero-band flags. A float32-cast model's value is a float: its key is exact.
+// A float64 model keys RD32(v) and decides ties on the double (exact_right).
+__device__ __forceinline__ void key_of(const ForestArgs& a, double v, int& k, bool& nan, bool& zero) {
+    if (a.cast_f32) {
+        const float f = __double2float_rn(v);
+        nan = f != f;
+        zero = nan || fabsf(f) <= 1e-35f;  // the float compare of kZeroThr's exact value
+        k = key32(f);
+    } else {
+        nan = v != v;
+        zero = nan || fabs(v) <= kZeroThr;
+        k = key32(__double2float_rd(v));
+    }
+}
+
+// put_keys with the key already made.
+template <int STRIDE>
+__device__ __forceinline__ void put_made_keys(int* col, int4 s, int k, bool nan, bool zero, int mask) {
+    auto tag = [mask](int key, int slot) { return (key & ~mask) | (slot & mask); };
+    if (s.x >= 0) col[s.x * STRIDE] = tag(nan ? INT_MAX : k, s.x);
+    if (s.y >= 0) col[s.y * STRIDE] = tag(nan ? INT_MIN : k, s.y);
+    if (s.z >= 0) col[s.z * STRIDE] = tag(zero ? INT_MAX : k, s.z);
+    if (s.w >= 0) col[s.w * STRIDE] = tag(zero ? INT_MIN : k, s.w);
+}
+
+// Keys of one row, this lane's, for features [f_begin, f_end), written to
+// col[slot * STRIDE]. The lane reads its own row eight values at a time, with
+// 16-byte vector loads when the rows are 16-byte aligned (the warp's 32 lanes
+// read 32 rows; the second half of each 32-byte sector comes from L1), so no
+// shared-memory transpose is needed; each value is prepared once (the float32
+// cast and key straight from the double when the model has no preprocessing)
+// and its key written to every variant slot its feature uses. Rows at or past
+// `batch` are prepared as 0.0: their walks read in-bounds shared memory and
+// their results are never stored.
+template <int STRIDE, typename XT>
+__device__ void prepare_own_row(const ForestArgs& a, const XT* __restrict__ x, long long row, long long batch, int* col,
+                                int f_begin, int f_end, int mask) {
+    constexpr int kBatch = 8;
+    constexpr int kVec = 16 / static_cast<int>(sizeof(XT));  // values per 16-byte load
+    const bool live = row < batch;
+    const XT* p = x + (live ? row : 0ll) * a.F;
+    const bool plain = !a.standardize && !a.clip;
+    const bool vec = a.F % kVec == 0 && f_begin % kVec == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    for (int f0 = f_begin; f0 < f_end; f0 += kBatch) {
+        const int n = min(kBatch, f_end - f0);
+        double v[kBatch];
+        if (vec && n == kBatch) {
+            if constexpr (sizeof(XT) == 8) {
+#pragma unroll
+                for (int i = 0; i < kBatch / 2; ++i) {
+                    const double2 t = __ldg(reinterpret_cast<const double2*>(p + f0) + i);
+                    v[2 * i] = t.x;
+                    v[2 * i + 1] = t.y;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kBatch / 4; ++i) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(p + f0) + i);
+                    v[4 * i] = t.x;
+                    v[4 * i + 1] = t.y;
+                    v[4 * i + 2] = t.z;
+                    v[4 * i + 3] = t.w;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) v[i] = i < n ? load_x(p + f0 + i) : 0.0;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            if (i < n) {
+                const int f = f0 + i;
+                double val = live ? v[i] : 0.0;
+                if (!plain) {
+                    const double mean = a.standardize ? __ldg(a.pre_mean + f) : 0.0;
+                    const double scale = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
+                    val = finish(a, val, mean, scale);
+                }
+                int k;
+                bool nan, zero;
+                key_of(a, val, k, nan, zero);
+                put_made_keys<STRIDE>(col, __ldg(a.slot_of + f), k, nan, zero, mask);
+            }
+        }
+    }
+}
+
 inline constexpr int kPrepTile = 4;                               // features per transpose tile
 inline constexpr int kPrepTileBytes = 32 * (kPrepTile + 1) * 8;  // one warp's tile
 
@@ -107,7 +199,7 @@ inline constexpr int kPrepTileBytes = 32 * (kPrepTile + 1) * 8;  // one warp's t
 // row's values into keys, column `lane` of the [slot][STRIDE] table at `keys`.
 template <int STRIDE, typename XT>
 __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long long row0, long long batch, int* keys,
-                             double* tile, int lane, int f_begin, int f_end, int low) {
+                             double* tile, int lane, int f_begin, int f_end, int mask) {
     constexpr int kPerLoad = 32 / kPrepTile;  // rows covered by one warp-wide load
     const int sub = lane / kPrepTile, f_in = lane % kPrepTile;
     auto load = [&](int f0, double (&v)[kPrepTile]) {
@@ -136,7 +228,7 @@ __device__ void prepare_rows(const ForestArgs& a, const XT* __restrict__ x, long
         __syncwarp();
         const int nf = min(kPrepTile, f_end - f0);
         for (int j = 0; j < nf; ++j) {
-            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kPrepTile + 1) + j], low);
+            put_keys<STRIDE>(a, keys + lane, __ldg(a.slot_of + f0 + j), tile[lane * (kPrepTile + 1) + j], mask);
         }
         __syncwarp();
     };

@@ -9,14 +9,16 @@
 //
 //     word = (T & ~mask) | slot          mask = 2^slot_bits - 1
 //
-// and the row's key table holds k' = k | mask for every finite key, so a
-// step is one signed compare, k' > word: exact whenever k and T differ in
-// their high bits. When they agree (a float32 within a relative 2^-(23 -
-// slot_bits) of the threshold: rare) the walk notes a tie for the tree, and
-// after the chunk's walk the tied trees are walked again with every tied
-// split decided by the reference's own comparison of the prepared double
-// against the file threshold. NaN and zero-band keys (INT32_MAX, INT32_MIN)
-// never tie with a threshold.
+// and the row's key table holds k' = (k & ~mask) | slot in every slot's row,
+// so a key read for a split has the split word's low bits: a step is one
+// signed compare, k' > word, exact whenever k and T differ in their high
+// bits, and k' == word is exactly the case where they agree (a float32
+// within a relative 2^-(23 - slot_bits) of the threshold: rare). The walk
+// notes such a tie for the tree (one predicated compare), and after the
+// chunk's walk the tied trees are walked again with every tied split
+// decided by the reference's own comparison of the prepared double against
+// the file threshold. NaN and zero-band keys (INT32_MAX, INT32_MIN with the
+// slot in the low bits) never tie with a threshold.
 //
 // Work split. A CTA owns R rows for the whole ensemble: their key tables
 // ([slot][R] int32, lane l always reading bank l) stay in shared memory. Four
@@ -55,7 +57,6 @@ namespace {
 constexpr int kTeams = 4;                              // teams of R threads, one 64-tree block each at a time
 constexpr int kTrees = 4;                              // trees per chunk = trees one thread walks side by side
 constexpr int kChunksPerBlock = kTreeBlock / kTrees;   // 16
-constexpr int kTileBytes = kPrepTileBytes;            // one warp's transpose tile in the prepare
 constexpr int kHeapSmemLimit = 227 * 1024;
 constexpr int kMaxSlotBits = 10;
 static_assert(kTreeBlock % kTrees == 0, "chunks never straddle a block of 64 trees");
@@ -67,8 +68,7 @@ __host__ __device__ constexpr int record_bytes(int depth, bool leaf32) {
 // Shared memory layout (byte offsets): header (mbarriers [team][2] at 0,
 // buffer-done counters [team][2] at 64, fills issued [team][2] at 96, abort
 // flag at 128) | keys [slots][R] int32 | block partials [2][team][R] double |
-// first buffers of the four teams | second buffers of the four teams. During the prepare the
-// second buffers (not yet refilled) hold the warps' transpose tiles.
+// first buffers of the four teams | second buffers of the four teams.
 struct Layout {
     int keys, parts, ring0, ring1, total;
 };
@@ -80,8 +80,7 @@ __host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, i
     l.ring0 = l.parts + align128(2 * kTeams * rows * 8);
     const int chunk = kTrees * record_bytes(depth, leaf32);
     l.ring1 = l.ring0 + align128(kTeams * chunk);
-    const int tiles = kTeams * (rows / 32) * kTileBytes;
-    l.total = l.ring1 + align128(max(kTeams * chunk, tiles));
+    l.total = l.ring1 + align128(kTeams * chunk);
     return l;
 }
 
@@ -133,7 +132,7 @@ __device__ __forceinline__ void walk_leaves(const ForestArgs& a, const HeapArgs&
         for (int t = 0; t < kTrees; ++t) k[t] = lds_s32(col + (n[t] & mask) * (R * 4));
 #pragma unroll
         for (int t = 0; t < kTrees; ++t) {
-            tie[t] |= static_cast<uint32_t>(k[t] ^ static_cast<int>(n[t])) <= mask;
+            tie[t] |= k[t] == static_cast<int>(n[t]);
             p[t] = 2 * p[t] + go_left[t] + (k[t] > static_cast<int>(n[t]) ? 4u : 0u);
         }
     }
@@ -233,25 +232,24 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
                   &team_bar[b]);
         atomicAdd(&fills[2 * team + b], 1u);
     };
-    if (producer && n_team > 0 && blockIdx.x < groups) issue(0);
+    if (producer && blockIdx.x < groups) {
+        if (n_team > 0) issue(0);
+        if (n_team > 1) issue(1);
+    }
 
     const uint32_t col = smem_u32(keys) + r * 4;  // this row's key column
     for (long long g = blockIdx.x; g < groups; g += gridDim.x) {
         const long long row0 = g * R;
         const long long row = row0 + r;
         {
-            // Prepare: warp w builds the keys of rows 32 (w % (R / 32)) .. + 31
-            // for the team's quarter of the features.
-            const int slice = warp % kWarpsPerTeam;
-            const int per = (a.F + kTeams - 1) / kTeams;
+            // Prepare: thread (team, r) builds the keys of row r for the team's
+            // quarter of the features (even-sized, so vector loads stay aligned).
+            const int per = ((a.F + kTeams - 1) / kTeams + 7) & ~7;
             const int f_begin = min(a.F, team * per), f_end = min(a.F, f_begin + per);
-            double* tile = reinterpret_cast<double*>(smem + L.ring1 + warp * kTileBytes);
-            prepare_rows<R>(a, x, row0 + slice * 32, batch, keys + slice * 32, tile, lane, f_begin, f_end,
-                            static_cast<int>(mask));
-            if (team == 0) keys[a.pad_slot * R + slice * 32 + lane] = INT_MIN;
+            prepare_own_row<R>(a, x, row, batch, keys + r, f_begin, f_end, static_cast<int>(mask));
+            if (team == 0) keys[a.pad_slot * R + r] = INT_MIN;
         }
         __syncthreads();
-        if (producer && n_team > 1) issue(1);
         if (tid == 0 && g + gridDim.x < groups) {  // the next group's rows into L2 while this one walks
             const long long r1 = row0 + static_cast<long long>(gridDim.x) * R;
             prefetch_l2(x + r1 * a.F, static_cast<size_t>(min(static_cast<long long>(R), batch - r1)) * row_bytes);
@@ -331,9 +329,12 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
             apply_link<1>(a, v, 1);
             out[row] = v[0];
         }
-        // Every team passed the last round's barrier, so the buffers and tiles
-        // are free: start the next group's first chunk.
-        if (producer && n_team > 0 && g + gridDim.x < groups) issue(0);
+        // Every team passed the last round's barrier, so both buffers are
+        // free: start the next group's first two chunks.
+        if (producer && g + gridDim.x < groups) {
+            if (n_team > 0) issue(0);
+            if (n_team > 1) issue(1);
+        }
         __syncthreads();  // keys and partials are rewritten by the next group
     }
 }
