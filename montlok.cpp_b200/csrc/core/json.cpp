@@ -1,299 +1,322 @@
+// JSON parser: a tokenizer and a table of open containers (no recursion, so
+// deep documents cannot exhaust the stack; the depth limit is a rule of the
+// format, not of this implementation).
 #include "json.hpp"
 
+#include <charconv>
+#include <clocale>
 #include <cmath>
 #include <cstdlib>
-#include <locale>
-#include <sstream>
 #include <stdexcept>
+#include <unordered_set>
 
 namespace mlk::json {
 
 namespace {
 
-const char* kind_text(Value::Kind k) noexcept {
-    switch (k) {
-        case Value::Kind::Null: return "null";
-        case Value::Kind::Bool: return "bool";
-        case Value::Kind::Number: return "number";
-        case Value::Kind::String: return "string";
-        case Value::Kind::Array: return "array";
-        case Value::Kind::Object: return "object";
-    }
-    return "?";
+constexpr size_t kMaxDepth = 128;  // a value may sit inside at most 128 containers
+
+[[noreturn]] void reject(size_t at, const std::string& why) {
+    throw std::runtime_error("malformed JSON (offset " + std::to_string(at) + "): " + why);
 }
 
-[[noreturn]] void wrong_kind(Value::Kind want, Value::Kind have) {
-    throw std::runtime_error(std::string("JSON value is ") + kind_text(have) + ", expected " + kind_text(want));
+enum class Tok : uint8_t { End, BeginObject, EndObject, BeginArray, EndArray, Colon, Comma, Str, Num, True, False, Null };
+
+// Splits the text into tokens; string tokens are unescaped into `text`,
+// number tokens converted into `number`.
+class Tokenizer {
+public:
+    explicit Tokenizer(std::string_view s) : s_(s) {}
+
+    size_t offset() const noexcept { return start_; }
+
+    Tok next(std::string& text, double& number) {
+        while (pos_ < s_.size() && (s_[pos_] == ' ' || s_[pos_] == '\n' || s_[pos_] == '\r' || s_[pos_] == '\t')) {
+            ++pos_;
+        }
+        start_ = pos_;
+        if (pos_ == s_.size()) return Tok::End;
+        const char c = s_[pos_];
+        switch (c) {
+            case '{': ++pos_; return Tok::BeginObject;
+            case '}': ++pos_; return Tok::EndObject;
+            case '[': ++pos_; return Tok::BeginArray;
+            case ']': ++pos_; return Tok::EndArray;
+            case ':': ++pos_; return Tok::Colon;
+            case ',': ++pos_; return Tok::Comma;
+            case '"': read_string(text); return Tok::Str;
+            case 't': literal("true"); return Tok::True;
+            case 'f': literal("false"); return Tok::False;
+            case 'n': literal("null"); return Tok::Null;
+            default:
+                if (c == '-' || (c >= '0' && c <= '9')) {
+                    number = read_number();
+                    return Tok::Num;
+                }
+                reject(pos_, std::string("unexpected character '") + c + "'");
+        }
+    }
+
+private:
+    void literal(std::string_view word) {
+        if (s_.substr(pos_, word.size()) != word) reject(pos_, "unknown literal");
+        pos_ += word.size();
+    }
+
+    size_t run_of_digits() noexcept {
+        const size_t from = pos_;
+        while (pos_ < s_.size() && s_[pos_] >= '0' && s_[pos_] <= '9') ++pos_;
+        return pos_ - from;
+    }
+
+    // number = [-] (0 | [1-9][0-9]*) [. [0-9]+] [(e|E) [+|-] [0-9]+]
+    double read_number() {
+        const size_t from = pos_;
+        if (s_[pos_] == '-') ++pos_;
+        if (pos_ < s_.size() && s_[pos_] == '0') {
+            ++pos_;
+        } else if (run_of_digits() == 0) {
+            reject(from, "a number needs digits");
+        }
+        if (pos_ < s_.size() && s_[pos_] == '.') {
+            ++pos_;
+            if (run_of_digits() == 0) reject(from, "a number needs digits after '.'");
+        }
+        if (pos_ < s_.size() && (s_[pos_] == 'e' || s_[pos_] == 'E')) {
+            ++pos_;
+            if (pos_ < s_.size() && (s_[pos_] == '+' || s_[pos_] == '-')) ++pos_;
+            if (run_of_digits() == 0) reject(from, "a number needs exponent digits");
+        }
+        double x = 0.0;
+        const char* first = s_.data() + from;
+        const char* last = s_.data() + pos_;
+        const auto [end, ec] = std::from_chars(first, last, x);
+        if (ec == std::errc::result_out_of_range) {
+            // Too large, or too small: a number below the smallest subnormal
+            // reads as the C library reads it (0 or the subnormal), as the
+            // reference loader does; only overflow is an error.
+            static const locale_t c_locale = newlocale(LC_ALL_MASK, "C", nullptr);
+            const std::string token(first, last);
+            x = strtod_l(token.c_str(), nullptr, c_locale);
+        } else if (ec != std::errc() || end != last) {
+            reject(from, "not a number");
+        }
+        if (!std::isfinite(x)) reject(from, "number does not fit a double");
+        return x;
+    }
+
+    unsigned hex_unit() {
+        if (s_.size() - pos_ < 4) reject(pos_, "short \\u escape");
+        unsigned u = 0;
+        for (int i = 0; i < 4; ++i) {
+            const char h = s_[pos_++];
+            const int d = (h >= '0' && h <= '9') ? h - '0'
+                        : (h >= 'a' && h <= 'f') ? h - 'a' + 10
+                        : (h >= 'A' && h <= 'F') ? h - 'A' + 10
+                                                 : -1;
+            if (d < 0) reject(pos_ - 1, "bad hex digit in \\u escape");
+            u = u * 16 + static_cast<unsigned>(d);
+        }
+        return u;
+    }
+
+    static void append_utf8(std::string& out, unsigned cp) {
+        if (cp < 0x80) {
+            out.push_back(static_cast<char>(cp));
+            return;
+        }
+        // Lead byte and continuation bytes, 6 payload bits each.
+        const int tail = cp < 0x800 ? 1 : cp < 0x10000 ? 2 : 3;
+        static const unsigned char lead[] = {0, 0xC0, 0xE0, 0xF0};
+        out.push_back(static_cast<char>(lead[tail] | (cp >> (6 * tail))));
+        for (int k = tail - 1; k >= 0; --k) out.push_back(static_cast<char>(0x80 | ((cp >> (6 * k)) & 0x3F)));
+    }
+
+    void read_string(std::string& out) {
+        out.clear();
+        const size_t open = pos_++;
+        for (;;) {
+            if (pos_ >= s_.size()) reject(open, "string never closed");
+            const auto c = static_cast<unsigned char>(s_[pos_++]);
+            if (c == '"') return;
+            if (c < 0x20) reject(pos_ - 1, "raw control character in string");
+            if (c != '\\') {
+                out.push_back(static_cast<char>(c));
+                continue;
+            }
+            if (pos_ >= s_.size()) reject(open, "string never closed");
+            const char e = s_[pos_++];
+            static const std::string_view simple = "\"\\/bfnrt", meaning = "\"\\/\b\f\n\r\t";
+            if (const size_t k = simple.find(e); k != std::string_view::npos) {
+                out.push_back(meaning[k]);
+                continue;
+            }
+            if (e != 'u') reject(pos_ - 1, "unknown escape");
+            unsigned cp = hex_unit();
+            if (cp >= 0xDC00 && cp <= 0xDFFF) reject(pos_ - 6, "low surrogate without a high one");
+            if (cp >= 0xD800 && cp <= 0xDBFF) {
+                if (s_.substr(pos_, 2) != "\\u") reject(pos_, "high surrogate without a low one");
+                pos_ += 2;
+                const unsigned low = hex_unit();
+                if (low < 0xDC00 || low > 0xDFFF) reject(pos_ - 6, "high surrogate without a low one");
+                cp = 0x10000 + (((cp & 0x3FF) << 10) | (low & 0x3FF));
+            }
+            append_utf8(out, cp);
+        }
+    }
+
+    std::string_view s_;
+    size_t pos_ = 0, start_ = 0;
+};
+
+// A container being filled: its members so far (objects also keep the
+// names seen and the name waiting for its value).
+struct Open {
+    bool object;
+    Array items;
+    Object members;
+    std::unordered_set<std::string> names;
+    std::string name;
+};
+
+}  // namespace
+
+Value Value::parse(std::string_view text) {
+    Tokenizer tokens(text);
+    std::vector<Open> open;
+    std::string str;
+    double num = 0.0;
+    Value root;
+    bool have_root = false;
+
+    // Where the grammar stands, per the innermost container: just opened,
+    // after a member name, after ':' or ',', or after a complete value.
+    enum class At { Start, Opened, Name, Colon, Comma, Value };
+    At at = At::Start;
+
+    // Hands a finished value to the innermost container, or makes it the root.
+    auto deliver = [&](Value v) {
+        if (open.empty()) {
+            root = std::move(v);
+            have_root = true;
+        } else if (open.back().object) {
+            open.back().members.emplace_back(std::move(open.back().name), std::move(v));
+        } else {
+            open.back().items.push_back(std::move(v));
+        }
+        at = At::Value;
+    };
+
+    for (;;) {
+        const Tok t = tokens.next(str, num);
+        const size_t where = tokens.offset();
+        if (have_root) {
+            if (t != Tok::End) reject(where, "text after the document");
+            return root;
+        }
+        const bool in_object = !open.empty() && open.back().object;
+        const bool value_ok = at == At::Start || at == At::Colon || (!in_object && (at == At::Opened || at == At::Comma));
+        const bool too_deep = open.size() > kMaxDepth;  // for a value arriving now
+        switch (t) {
+            case Tok::End: reject(where, "document ends early");
+            case Tok::BeginObject:
+            case Tok::BeginArray:
+                if (!value_ok) reject(where, "a value is not allowed here");
+                if (too_deep) reject(where, "containers nested too deep");
+                open.push_back(Open{t == Tok::BeginObject, {}, {}, {}, {}});
+                at = At::Opened;
+                break;
+            case Tok::EndObject:
+            case Tok::EndArray: {
+                const bool closes_object = t == Tok::EndObject;
+                if (open.empty() || open.back().object != closes_object || !(at == At::Opened || at == At::Value)) {
+                    reject(where, "unexpected closing bracket");
+                }
+                Open done = std::move(open.back());
+                open.pop_back();
+                deliver(done.object ? Value(std::move(done.members)) : Value(std::move(done.items)));
+                break;
+            }
+            case Tok::Colon:
+                if (!in_object || at != At::Name) reject(where, "unexpected ':'");
+                at = At::Colon;
+                break;
+            case Tok::Comma:
+                if (open.empty() || at != At::Value) reject(where, "unexpected ','");
+                at = At::Comma;
+                break;
+            case Tok::Str:
+                if (in_object && (at == At::Opened || at == At::Comma)) {
+                    if (!open.back().names.insert(str).second) reject(where, "member \"" + str + "\" named twice");
+                    open.back().name = str;
+                    at = At::Name;
+                    break;
+                }
+                if (!value_ok) reject(where, "a value is not allowed here");
+                if (too_deep) reject(where, "containers nested too deep");
+                deliver(Value(str));
+                break;
+            case Tok::Num:
+            case Tok::True:
+            case Tok::False:
+            case Tok::Null:
+                if (!value_ok) reject(where, "a value is not allowed here");
+                if (too_deep) reject(where, "containers nested too deep");
+                deliver(t == Tok::Num ? Value(num) : t == Tok::Null ? Value() : Value(t == Tok::True));
+                break;
+        }
+    }
 }
 
-void put_utf8(std::string& out, uint32_t c) {
-    if (c < 0x80) {
-        out += static_cast<char>(c);
-    } else if (c < 0x800) {
-        out += static_cast<char>(0xC0 | (c >> 6));
-        out += static_cast<char>(0x80 | (c & 0x3F));
-    } else if (c < 0x10000) {
-        out += static_cast<char>(0xE0 | (c >> 12));
-        out += static_cast<char>(0x80 | ((c >> 6) & 0x3F));
-        out += static_cast<char>(0x80 | (c & 0x3F));
-    } else {
-        out += static_cast<char>(0xF0 | (c >> 18));
-        out += static_cast<char>(0x80 | ((c >> 12) & 0x3F));
-        out += static_cast<char>(0x80 | ((c >> 6) & 0x3F));
-        out += static_cast<char>(0x80 | (c & 0x3F));
-    }
+namespace {
+
+const char* kind_name(Value::Kind k) noexcept {
+    static const char* names[] = {"null", "a boolean", "a number", "a string", "an array", "an object"};
+    return names[static_cast<int>(k)];
+}
+
+[[noreturn]] void not_a(Value::Kind want, Value::Kind got) {
+    throw std::runtime_error(std::string("expected ") + kind_name(want) + " in JSON, found " + kind_name(got));
 }
 
 }  // namespace
 
-// A recursive-descent reader over one document.
-class Reader {
-public:
-    explicit Reader(std::string_view s) : s_(s) {}
-
-    Value document() {
-        blank();
-        Value v = value(0);
-        blank();
-        if (i_ != s_.size()) error("trailing characters");
-        return v;
-    }
-
-private:
-    static constexpr int kDeepest = 128;
-
-    [[noreturn]] void error(const char* what) const {
-        throw std::runtime_error("invalid JSON at byte " + std::to_string(i_) + ": " + what);
-    }
-
-    bool at_end() const noexcept { return i_ >= s_.size(); }
-    char peek() const noexcept { return s_[i_]; }
-
-    void blank() noexcept {
-        while (!at_end() && (peek() == ' ' || peek() == '\t' || peek() == '\n' || peek() == '\r')) ++i_;
-    }
-
-    bool take(char c) noexcept {
-        if (!at_end() && peek() == c) {
-            ++i_;
-            return true;
-        }
-        return false;
-    }
-
-    void word(std::string_view w) {
-        if (s_.compare(i_, w.size(), w) != 0) error("unexpected token");
-        i_ += w.size();
-    }
-
-    Value value(int depth) {
-        if (depth > kDeepest) error("nesting too deep");
-        if (at_end()) error("unexpected end");
-        Value v;
-        switch (peek()) {
-            case 'n': word("null"); return v;
-            case 't':
-                word("true");
-                v.kind_ = Value::Kind::Bool;
-                v.flag_ = true;
-                return v;
-            case 'f':
-                word("false");
-                v.kind_ = Value::Kind::Bool;
-                return v;
-            case '"':
-                v.kind_ = Value::Kind::String;
-                v.text_ = string();
-                return v;
-            case '[': return array(depth);
-            case '{': return object(depth);
-            default: return number();
-        }
-    }
-
-    void digits() noexcept {
-        while (!at_end() && peek() >= '0' && peek() <= '9') ++i_;
-    }
-
-    Value number() {
-        const size_t begin = i_;
-        take('-');
-        if (at_end()) error("bad number");
-        if (peek() == '0') {
-            ++i_;
-        } else if (peek() >= '1' && peek() <= '9') {
-            digits();
-        } else {
-            error("bad number");
-        }
-        if (take('.')) {
-            const size_t d = i_;
-            digits();
-            if (i_ == d) error("bad fraction");
-        }
-        if (!at_end() && (peek() == 'e' || peek() == 'E')) {
-            ++i_;
-            if (!take('+')) take('-');
-            const size_t d = i_;
-            digits();
-            if (i_ == d) error("bad exponent");
-        }
-        // The grammar is checked; the conversion is locale-independent.
-        std::istringstream in(std::string(s_.substr(begin, i_ - begin)));
-        in.imbue(std::locale::classic());
-        double x = 0;
-        in >> x;
-        if (in.fail() || !std::isfinite(x)) error("number out of range");
-        Value v;
-        v.kind_ = Value::Kind::Number;
-        v.number_ = x;
-        return v;
-    }
-
-    uint32_t hex4() {
-        if (i_ + 4 > s_.size()) error("bad unicode escape");
-        uint32_t c = 0;
-        for (int k = 0; k < 4; ++k) {
-            const char h = s_[i_++];
-            c <<= 4;
-            if (h >= '0' && h <= '9') c |= static_cast<uint32_t>(h - '0');
-            else if (h >= 'a' && h <= 'f') c |= static_cast<uint32_t>(h - 'a' + 10);
-            else if (h >= 'A' && h <= 'F') c |= static_cast<uint32_t>(h - 'A' + 10);
-            else error("bad unicode escape");
-        }
-        return c;
-    }
-
-    std::string string() {
-        ++i_;
-        std::string out;
-        for (;;) {
-            if (at_end()) error("unterminated string");
-            const auto c = static_cast<unsigned char>(s_[i_++]);
-            if (c == '"') return out;
-            if (c < 0x20) error("control character in string");
-            if (c != '\\') {
-                out += static_cast<char>(c);
-                continue;
-            }
-            if (at_end()) error("unterminated escape");
-            const char e = s_[i_++];
-            switch (e) {
-                case '"': out += '"'; break;
-                case '\\': out += '\\'; break;
-                case '/': out += '/'; break;
-                case 'b': out += '\b'; break;
-                case 'f': out += '\f'; break;
-                case 'n': out += '\n'; break;
-                case 'r': out += '\r'; break;
-                case 't': out += '\t'; break;
-                case 'u': {
-                    uint32_t c1 = hex4();
-                    if (c1 >= 0xDC00 && c1 <= 0xDFFF) error("unpaired surrogate");
-                    if (c1 >= 0xD800 && c1 <= 0xDBFF) {
-                        if (!(take('\\') && take('u'))) error("unpaired surrogate");
-                        const uint32_t c2 = hex4();
-                        if (c2 < 0xDC00 || c2 > 0xDFFF) error("unpaired surrogate");
-                        c1 = 0x10000 + ((c1 - 0xD800) << 10) + (c2 - 0xDC00);
-                    }
-                    put_utf8(out, c1);
-                    break;
-                }
-                default: error("bad escape");
-            }
-        }
-    }
-
-    Value array(int depth) {
-        ++i_;
-        auto items = std::make_shared<Array>();
-        blank();
-        if (!take(']')) {
-            for (;;) {
-                blank();
-                items->push_back(value(depth + 1));
-                blank();
-                if (take(']')) break;
-                if (!take(',')) error("expected ',' or ']'");
-            }
-        }
-        Value v;
-        v.kind_ = Value::Kind::Array;
-        v.items_ = std::move(items);
-        return v;
-    }
-
-    Value object(int depth) {
-        ++i_;
-        auto members = std::make_shared<Object>();
-        blank();
-        if (!take('}')) {
-            for (;;) {
-                blank();
-                if (at_end() || peek() != '"') error("expected member name");
-                std::string key = string();
-                for (const auto& m : *members) {
-                    if (m.first == key) error("duplicate member name");
-                }
-                blank();
-                if (!take(':')) error("expected ':'");
-                blank();
-                Value item = value(depth + 1);
-                members->emplace_back(std::move(key), std::move(item));
-                blank();
-                if (take('}')) break;
-                if (!take(',')) error("expected ',' or '}'");
-            }
-        }
-        Value v;
-        v.kind_ = Value::Kind::Object;
-        v.members_ = std::move(members);
-        return v;
-    }
-
-    std::string_view s_;
-    size_t i_ = 0;
-};
-
-Value Value::parse(std::string_view text) { return Reader(text).document(); }
-
 bool Value::as_bool() const {
-    if (kind_ != Kind::Bool) wrong_kind(Kind::Bool, kind_);
-    return flag_;
+    if (!is_bool()) not_a(Kind::Bool, kind());
+    return std::get<bool>(data_);
 }
 
 double Value::as_number() const {
-    if (kind_ != Kind::Number) wrong_kind(Kind::Number, kind_);
-    return number_;
+    if (!is_number()) not_a(Kind::Number, kind());
+    return std::get<double>(data_);
 }
 
 int64_t Value::as_int() const {
     const double x = as_number();
-    if (std::nearbyint(x) != x || std::fabs(x) > 9007199254740992.0) {
-        throw std::runtime_error("JSON number is not an exact integer");
-    }
+    constexpr double kExact = 9007199254740992.0;  // 2^53
+    if (!(std::fabs(x) <= kExact) || std::trunc(x) != x) throw std::runtime_error("JSON number is not an integer");
     return static_cast<int64_t>(x);
 }
 
 const std::string& Value::as_string() const {
-    if (kind_ != Kind::String) wrong_kind(Kind::String, kind_);
-    return text_;
+    if (!is_string()) not_a(Kind::String, kind());
+    return std::get<std::string>(data_);
 }
 
 const Array& Value::as_array() const {
-    if (kind_ != Kind::Array) wrong_kind(Kind::Array, kind_);
-    return *items_;
+    if (!is_array()) not_a(Kind::Array, kind());
+    return *std::get<std::shared_ptr<const Array>>(data_);
 }
 
 const Object& Value::as_object() const {
-    if (kind_ != Kind::Object) wrong_kind(Kind::Object, kind_);
-    return *members_;
+    if (!is_object()) not_a(Kind::Object, kind());
+    return *std::get<std::shared_ptr<const Object>>(data_);
 }
 
 const Value* Value::find(std::string_view key) const noexcept {
-    if (kind_ != Kind::Object) return nullptr;
-    for (const auto& m : *members_) {
-        if (m.first == key) return &m.second;
+    if (!is_object()) return nullptr;
+    for (const auto& [name, value] : *std::get<std::shared_ptr<const Object>>(data_)) {
+        if (name == key) return &value;
     }
     return nullptr;
 }

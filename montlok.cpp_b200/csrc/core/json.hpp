@@ -1,9 +1,12 @@
-// Strict JSON (RFC 8259) values for safetensors headers and model specs.
+// JSON values for safetensors headers and model specs.
 //
-// Acceptance follows the reference loader (montlok.cpp src/core/json.cpp):
-// duplicate member names, unpaired surrogates, control characters in strings,
-// nesting deeper than 128 and numbers that do not fit a finite double are
-// errors; integers are "exact" when integral with magnitude <= 2^53.
+// The parser accepts RFC 8259 documents only and additionally refuses what a
+// model file must never contain, so that the same files are accepted as by
+// the reference loader: an object that names a member twice, a \u escape
+// that is half of a surrogate pair, a raw control character inside a string,
+// containers nested more than 128 deep, and numbers that overflow (or
+// underflow) a double. A number counts as an integer when it is integral and
+// at most 2^53 in magnitude.
 #pragma once
 
 #include <cstdint>
@@ -11,33 +14,39 @@
 #include <string>
 #include <string_view>
 #include <utility>
+#include <variant>
 #include <vector>
 
 namespace mlk::json {
 
 class Value;
 using Array = std::vector<Value>;
-using Object = std::vector<std::pair<std::string, Value>>;
+using Object = std::vector<std::pair<std::string, Value>>;  // members in document order
 
 class Value {
 public:
     enum class Kind : uint8_t { Null, Bool, Number, String, Array, Object };
 
     Value() = default;
+    explicit Value(bool b) : data_(b) {}
+    explicit Value(double x) : data_(x) {}
+    explicit Value(std::string s) : data_(std::move(s)) {}
+    explicit Value(Array items) : data_(std::make_shared<const json::Array>(std::move(items))) {}
+    explicit Value(Object members) : data_(std::make_shared<const json::Object>(std::move(members))) {}
 
-    // Parses a whole document; throws std::runtime_error naming the byte
+    // Parses one whole document; throws std::runtime_error with the byte
     // offset of the first problem.
     static Value parse(std::string_view text);
 
-    Kind kind() const noexcept { return kind_; }
-    bool is_null() const noexcept { return kind_ == Kind::Null; }
-    bool is_bool() const noexcept { return kind_ == Kind::Bool; }
-    bool is_number() const noexcept { return kind_ == Kind::Number; }
-    bool is_string() const noexcept { return kind_ == Kind::String; }
-    bool is_array() const noexcept { return kind_ == Kind::Array; }
-    bool is_object() const noexcept { return kind_ == Kind::Object; }
+    Kind kind() const noexcept { return static_cast<Kind>(data_.index()); }
+    bool is_null() const noexcept { return kind() == Kind::Null; }
+    bool is_bool() const noexcept { return kind() == Kind::Bool; }
+    bool is_number() const noexcept { return kind() == Kind::Number; }
+    bool is_string() const noexcept { return kind() == Kind::String; }
+    bool is_array() const noexcept { return kind() == Kind::Array; }
+    bool is_object() const noexcept { return kind() == Kind::Object; }
 
-    // Each throws std::runtime_error when the value has another kind.
+    // Each throws std::runtime_error when the value is of another kind.
     bool as_bool() const;
     double as_number() const;
     int64_t as_int() const;  // integral and |x| <= 2^53, else throws
@@ -49,13 +58,10 @@ public:
     const Value* find(std::string_view key) const noexcept;
 
 private:
-    friend class Reader;
-    Kind kind_ = Kind::Null;
-    bool flag_ = false;
-    double number_ = 0;
-    std::string text_;
-    std::shared_ptr<const Array> items_;
-    std::shared_ptr<const Object> members_;
+    // Alternatives in the order of Kind.
+    std::variant<std::monostate, bool, double, std::string, std::shared_ptr<const json::Array>,
+                 std::shared_ptr<const json::Object>>
+        data_;
 };
 
 }  // namespace mlk::json

@@ -277,18 +277,8 @@ def from_lightgbm(model: Any, *, feature_names: Sequence[str] | None = None,
         raise ValueError("linear trees are not supported")
     features = int(dump["max_feature_idx"]) + 1
     per_round = int(dump.get("num_tree_per_iteration", 1))
-    words = str(dump.get("objective", "regression")).split()
-    kind = words[0] if words else "regression"
-    params = dict(w.split(":", 1) for w in words[1:] if ":" in w)
-    link, scale = "identity", 1.0
-    if kind in ("binary", "cross_entropy", "xentropy"):
-        link, scale = "sigmoid", float(params.get("sigmoid", 1.0))
-    elif kind in ("multiclass", "softmax"):
-        link = "softmax"
-    elif kind in ("poisson", "gamma", "tweedie"):
-        link = "exp"
-    elif kind in ("multiclassova", "multiclass_ova", "ova", "ovr"):
-        raise ValueError("one-vs-all multiclass objectives are not supported")
+    objective = str(dump.get("objective", "regression"))
+    link, scale = _lightgbm_link(objective)
 
     def split_of(node):
         if "split_feature" not in node:
@@ -310,11 +300,42 @@ def from_lightgbm(model: Any, *, feature_names: Sequence[str] | None = None,
     return tree_ensemble(nodes, roots, tree_outputs, features=features, outputs=per_round, link=link,
                          sigmoid_scale=scale, aggregate="mean" if dump.get("average_output") else "sum",
                          feature_names=names,
-                         metadata={"source": "lightgbm", "objective": " ".join(words), **(metadata or {})})
+                         metadata={"source": "lightgbm", "objective": " ".join(objective.split()), **(metadata or {})})
 
 
-_XGB_LOGISTIC = ("binary:logistic", "reg:logistic")
-_XGB_LOG = ("count:poisson", "reg:gamma", "reg:tweedie", "survival:cox")
+# The link LightGBM's predict() applies to the raw sum, by objective family
+# (the first word of the dump's "objective"; "sigmoid:<k>" scales the
+# logistic). One-vs-all multiclass has a per-class sigmoid: not representable.
+_LGB_LINKS = {"binary": "sigmoid", "cross_entropy": "sigmoid", "xentropy": "sigmoid", "multiclass": "softmax",
+              "softmax": "softmax", "poisson": "exp", "gamma": "exp", "tweedie": "exp"}
+_LGB_ONE_VS_ALL = {"multiclassova", "multiclass_ova", "ova", "ovr"}
+
+
+def _lightgbm_link(objective: str) -> tuple[str, float]:
+    family, *options = objective.split() or ["regression"]
+    if family in _LGB_ONE_VS_ALL:
+        raise ValueError("one-vs-all multiclass objectives are not supported")
+    link = _LGB_LINKS.get(family, "identity")
+    settings = {key: value for key, sep, value in (o.partition(":") for o in options) if sep}
+    return link, float(settings.get("sigmoid", 1.0)) if link == "sigmoid" else 1.0
+
+
+# XGBoost objectives whose prediction is not the raw margin: the link on the
+# summed margin, and how base_score (a prediction) turns into a margin.
+_XGB_OBJECTIVES = {
+    "binary:logistic": ("sigmoid", lambda p: math.log(p / (1.0 - p))),
+    "reg:logistic": ("sigmoid", lambda p: math.log(p / (1.0 - p))),
+    "count:poisson": ("exp", math.log),
+    "reg:gamma": ("exp", math.log),
+    "reg:tweedie": ("exp", math.log),
+    "survival:cox": ("exp", math.log),
+}
+
+
+def _xgboost_link(objective: str) -> tuple[str, Any]:
+    if objective in _XGB_OBJECTIVES:
+        return _XGB_OBJECTIVES[objective]
+    return ("softmax" if objective.startswith("multi:") else "identity"), float
 
 
 def from_xgboost(model: Any, *, features: int | None = None, objective: str | None = None,
@@ -343,14 +364,8 @@ def from_xgboost(model: Any, *, features: int | None = None, objective: str | No
         dumps = list(model)
     if features is None or objective is None or (base_score is None and base_margin is None):
         raise ValueError("tree dumps need features=, objective= and base_score= or base_margin=")
-    if base_margin is not None:
-        margin = base_margin
-    elif objective in _XGB_LOGISTIC:
-        margin = math.log(float(base_score) / (1.0 - float(base_score)))
-    elif objective in _XGB_LOG:
-        margin = math.log(float(base_score))
-    else:
-        margin = float(base_score)
+    link, to_margin = _xgboost_link(objective)
+    margin = base_margin if base_margin is not None else to_margin(float(base_score))
     outputs = classes if classes and classes > 1 else 1
     by_name = {str(n): i for i, n in enumerate(feature_names)} if feature_names else {}
 
@@ -377,13 +392,6 @@ def from_xgboost(model: Any, *, features: int | None = None, objective: str | No
         roots.append(len(nodes.feature))
         tree_outputs.append((t // parallel_trees) % outputs)
         _append_dump_tree(nodes, tree, split_of, lambda n: float(n["leaf"]))
-    link = "identity"
-    if objective in _XGB_LOGISTIC:
-        link = "sigmoid"
-    elif objective.startswith("multi:"):
-        link = "softmax"
-    elif objective in _XGB_LOG:
-        link = "exp"
     return tree_ensemble(nodes, roots, tree_outputs, features=int(features), outputs=outputs, decision="lt",
                          feature_cast="f32", link=link, base_score=margin, feature_names=feature_names,
                          metadata={"source": "xgboost", "objective": objective, **(metadata or {})})

@@ -1,6 +1,6 @@
-"""The `montlok` command line (python -m montlok): info, convert, env and the
-argument surface on CPU; predict and bench (host, pinned and device memory)
-on a GPU."""
+"""The `montlok` command line (python -m montlok): the argument surface and
+table reading on CPU; predict and bench (host, pinned and device memory) on
+a GPU."""
 
 from __future__ import annotations
 
@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 from forests import random_model, same_bits
-from golden.make_golden import lightgbm_dump
+import montlok
 from montlok import cli, export
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -25,23 +25,30 @@ def run(*argv: str) -> subprocess.CompletedProcess:
                           timeout=300)
 
 
-def test_info_and_convert(tmp_path):
-    dump = tmp_path / "model.json"
-    dump.write_text(json.dumps(lightgbm_dump("multiclass num_class:3", 3, 12, 5, seed=4)))
-    out = tmp_path / "model.montlok"
-    r = run("convert", str(dump), "-o", str(out))
-    assert r.returncode == 0, r.stderr
-    assert out.exists() and "tree_ensemble" in r.stdout
-    r = run("info", str(out))
-    assert r.returncode == 0, r.stderr
-    assert "features" in r.stdout
-    r = run("info", str(out), "--json")
-    assert json.loads(r.stdout)["family"] == "tree_ensemble"
+def test_version_without_a_gpu():
+    r = run("--version")
+    assert r.returncode == 0 and "montlok" in r.stdout
 
 
-def test_env_runs_without_a_gpu():
-    r = run("env")
-    assert r.returncode == 0 and "montlok" in r.stdout and "gpus" in r.stdout
+def test_csv_tables_match_columns_by_name(tmp_path):
+    """A CSV header is matched against the model's feature names."""
+    model = montlok.load(export.tree_ensemble(_nodes(), [0], [0], features=3,
+                                              feature_names=["a", "b", "c"]).to_bytes())
+    path = tmp_path / "x.csv"
+    path.write_text("c,a,b\n3,1,2\n6,4,\n")
+    table, names = cli._table(path)
+    assert names == ["c", "a", "b"]
+    x = cli._arrange(model, table, names)
+    np.testing.assert_array_equal(x[0], [1.0, 2.0, 3.0])
+    assert np.isnan(x[1, 1]) and x[1, 0] == 4.0 and x[1, 2] == 6.0
+
+
+def _nodes():
+    nodes = export.Nodes()
+    root = nodes.add(feature=0, threshold=0.5, flags=1 | (1 << 1))
+    nodes.left[root] = nodes.add(value=1.0)
+    nodes.right[root] = nodes.add(value=2.0)
+    return nodes
 
 
 def test_bench_and_predict_options_parse():
@@ -76,3 +83,7 @@ def test_bench_memory_modes(gpu, tmp_path, memory):
             memory)
     assert r.returncode == 0, r.stderr
     assert f"{memory} memory" in r.stdout and "p50" in r.stdout
+    r = run("bench", str(tmp_path / "m.montlok"), "--batch", "8", "--iterations", "100", "--memory", memory, "--json")
+    assert r.returncode == 0, r.stderr
+    report = json.loads(r.stdout)
+    assert report["memory"] == memory and report["p50_us"] > 0 and report["kernel"]

@@ -156,3 +156,53 @@ def test_no_cpu_fallback_without_a_gpu():
     model = tiny().load()
     with pytest.raises(RuntimeError, match="CUDA"):
         model.predict(np.zeros((4, 3)))
+
+
+# JSON edge cases placed inside a model spec (as the value of a metadata
+# field), so the spec parser meets them; each must be accepted or rejected
+# exactly as the reference runtime (compiled from its sources) does.
+JSON_EDGES = [
+    "1", "-0", "0.5e1", "1E+2", "1e-2", "123456789012345678901234567890", "1e308", "1e309", "-1e309", "1e-400",
+    "01", "1.", ".5", "1e", "-", "+1", "0x10", "NaN", "Infinity",
+    '"plain"', '"\\u00e9\\u4e2d"', '"\\ud83d\\ude00"', '"\\ud800"', '"\\udc00"', '"\\ud800x"', '"\\ud800\\u0041"',
+    '"tab\\there"', '"\\x41"', '"\\U0041"', '"raw\x01control"', '"raw\x7fdel"', '"\xc3\xa9"',
+    "true", "false", "null", "True", "nul", "[]", "{}", "[1,2,]", "[,1]", "[1 2]", '{"a":1,}', '{"a" 1}',
+    '{"a":1,"a":2}', '{"a":{"b":1,"b":2}}', '{"":1}', '[[[[]]]]', "\f1", " 1 ", "[1]]", "{1:2}",
+    "[" * 126 + "]" * 126, "[" * 127 + "]" * 127, "[" * 128 + "]" * 128, "[" * 127 + "1" + "]" * 127,
+    "[" * 126 + "1" + "]" * 126, "[" * 400 + "]" * 400,
+]
+
+
+def spec_with_edge(text: str) -> bytes:
+    import json as _json
+
+    data = tiny().to_bytes()
+    n = struct.unpack("<Q", data[:8])[0]
+    header = _json.loads(data[8:8 + n])
+    spec_text = header["__metadata__"]["montlok"]
+    assert spec_text.endswith("}")
+    edited = spec_text[:-1] + ',"x-edge":' + text + "}"
+    header["__metadata__"]["montlok"] = edited
+    raw = _json.dumps(header, separators=(",", ":")).encode()
+    raw += b" " * (-len(raw) % 8)
+    return struct.pack("<Q", len(raw)) + raw + data[8 + n:]
+
+
+@pytest.mark.parametrize("edge", JSON_EDGES, ids=range(len(JSON_EDGES)))
+def test_spec_json_is_read_like_the_reference(edge):
+    import oracle
+
+    if not oracle.available_reference():
+        pytest.skip("the reference library (oracle/_ref) was not built here")
+    model = spec_with_edge(edge)
+    try:
+        oracle.Reference().close(oracle.Reference().open(model))
+        reference_accepts = True
+    except ValueError:
+        reference_accepts = False
+    try:
+        montlok.load(model)
+        ours = True
+    except (ValueError, NotImplementedError):
+        ours = False
+    assert ours == reference_accepts
