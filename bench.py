@@ -169,14 +169,17 @@ def cpu_reference_rate(model: bytes, x: np.ndarray, seconds: float, threads: int
     return {"value": rows / elapsed, "unit": "rows/s", "cores": threads, "kind": kind, "sample": what}
 
 
-def reference_latency(calls: int, seconds: float, model: bytes, x: np.ndarray, threads: int) -> dict:
-    """Per-call latency of the reference runtime ({} without it)."""
+def reference_latency(calls: int, seconds: float, model: bytes, x: np.ndarray, threads: int,
+                      latency_threads: int = 0) -> dict:
+    """Per-call latency of the reference runtime ({} without it), with
+    `latency_threads` of its spinning single-row workers."""
     import oracle
 
     if not oracle.available_reference():
         return {}
     ref = oracle.Reference()
     ref.set_threads(threads)
+    ref.lib.montlok_set_latency_threads(int(latency_threads))
     h = ref.open(model)
     stats = {}
     try:
@@ -186,6 +189,7 @@ def reference_latency(calls: int, seconds: float, model: bytes, x: np.ndarray, t
             stats[str(n)] = latency_stats(ref.time_calls(h, rows, n, count, max(10, count // 10)))
     finally:
         ref.close(h)
+        ref.lib.montlok_set_latency_threads(0)
     return stats
 
 
@@ -397,15 +401,29 @@ def latency_figures(torch, montlok, cfg, args, cpu: bool) -> dict:
         model.predict_device(xd.data_ptr(), 64, od.data_ptr(), montlok._core.FLOAT64, stream.cuda_stream)
     end.record(stream)
     torch.cuda.synchronize()
-    fig = {"latency": stats, "kernel": {str(n): model.kernel(n) for n in LATENCY_SIZES},
+    # With latency threads on, calls of at most 8 rows go to the resident
+    # latency engine instead of a graph launch.
+    montlok.set_latency_threads(1)
+    engine = {}
+    try:
+        for n in (1, 8):
+            rows = x[: len(x) // n * n].reshape(-1, n * model.features)
+            samples, _ = montlok._core.bench(model, rows, batch=n, iterations=args.calls)
+            engine[str(n)] = latency_stats(samples)
+    finally:
+        montlok.set_latency_threads(0)
+    fig = {"latency": stats, "latency_engine": engine, "kernel": {str(n): model.kernel(n) for n in LATENCY_SIZES},
            "device_us_per_64_rows": start.elapsed_time(end) * 10.0,
            "gpu_launches": args.calls * len(LATENCY_SIZES)}
     if cpu:
         threads = os.cpu_count() or 1
         ref = reference_latency(args.calls, args.cpu_seconds, model_bytes, x, threads)
         if ref:
+            spin = min(7, max(1, threads - 1))
             fig["cpu_baseline"] = {"value": ref["64"]["p50_us"], "unit": "us", "cores": threads, "kind": "reference",
-                                   "sample": "per-call latency, calls of 1, 8 and 64 rows", "latency": ref}
+                                   "sample": "per-call latency, calls of 1, 8 and 64 rows", "latency": ref,
+                                   f"latency_with_{spin}_latency_threads":
+                                       reference_latency(args.calls, args.cpu_seconds, model_bytes, x, threads, spin)}
     return fig
 
 
@@ -422,6 +440,7 @@ def run_latency(args, cfg) -> None:
     fig = latency_figures(torch, montlok, cfg, args, cpu=not args.no_cpu)
     line = latency_line(args, cfg, fig["latency"])
     line["device_us_per_64_rows"] = fig["device_us_per_64_rows"]
+    line["latency_engine"] = fig["latency_engine"]
     line["kernel"] = fig["kernel"]
     line["e2e"] = {"value": fig["latency"]["64"]["p50_us"], "unit": "us", "h2d_bytes_per_step": 64 * 200 * 8,
                    "d2h_bytes_per_step": 64 * 8}

@@ -50,6 +50,7 @@ int threads() noexcept {
 void set_latency_threads(int threads) {
     if (threads < 0 || threads > 256) fail(Status::InvalidArgument, "latency threads must be in [0, 256]");
     g_latency_threads.store(threads);
+    mlk_cuda_set_latency_engine(threads > 0 ? 1 : 0);
 }
 
 int latency_threads() noexcept { return g_latency_threads.load(); }

@@ -1,0 +1,475 @@
+// Latency engine: a resident kernel that answers small host-buffer predicts
+// (at most kEngineRows rows) without a launch or a copy per call. It is the
+// GPU counterpart of the reference's latency threads (montlok_set_latency_
+// threads, src/core/runtime.cpp:300-420): workers that stay up, wait on a
+// mailbox and split a small batch's 64-tree blocks, whose sums are then added
+// in block order (trees.cpp:303-362).
+//
+// Each CTA of the engine owns one 64-tree block of a complete-tree forest and
+// keeps its tree records in shared memory for its whole life, so a walk is
+// eight shared loads. The calling thread writes the request's rows into a
+// mailbox in pinned host memory and bumps its sequence number. Thread 0 of
+// CTA 0 polls that number (system-scope acquire loads; the only poller of the
+// bus), CTA 0 reads the rows over the bus in 16-byte loads and relays them
+// through device memory, publishing the number in a device-memory word the
+// other CTAs poll. Every CTA then builds the rows' keys, walks its 64 trees
+// for each row (one thread per tree and row pair) and adds the leaves in tree
+// order into its block's partial sum. The last CTA to finish (a device-scope
+// counter, no waiting) adds the block sums in block order, applies the link
+// and writes each row's answer into the mailbox as one 16-byte record with
+// the request's number; the caller spins on those numbers.
+//
+// Every wait is bounded. An engine CTA exits when the host asks (stop), when
+// CTA 0 has seen no request for kEngineIdleNs (it raises a quit flag the
+// others follow; they also leave after twice that) or after kEnginePolls
+// polls. The host starts the engine on
+// demand with a cooperative launch (all CTAs resident, or the launch fails
+// and the call takes the graph path), relaunches it when it has exited, and
+// gives up on a request after kEngineTimeoutNs with MONTLOK_ERROR_INTERNAL.
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <thread>
+
+#include "async_copy.cuh"
+#include "device_common.cuh"
+#include "engine.cuh"
+#include "forest.cuh"
+
+namespace mlk::cuda {
+namespace {
+
+constexpr int kEngineThreads = 256;                     // 64 trees x 4 row pairs
+constexpr int kEnginePairs = kEngineThreads / kTreeBlock;
+constexpr unsigned long long kEngineIdleNs = 200000000ull;  // an engine idle this long exits
+constexpr long long kEnginePolls = 1ll << 24;               // hard cap on one wait's polls
+constexpr long long kEngineTimeoutNs = 2000000000ll;        // a request unanswered this long fails
+constexpr long long kEngineCheckNs = 20000000ll;            // when the host first checks the engine
+static_assert(kEngineRows == 2 * kEnginePairs, "each thread walks two rows");
+
+// The mailbox, in pinned host memory the engine reads and writes over the bus.
+struct Mailbox {
+    unsigned int seq;   // host: number of the latest request
+    unsigned int done;  // engine: unused (answers carry their own number)
+    unsigned int stop;  // host: exit now
+    int rows;           // host: rows of the latest request
+};
+
+// One row's answer, written with a single 16-byte store: the caller reads
+// `value` once `seq` shows its request's number, so the engine needs no
+// system-wide fence before publishing.
+struct alignas(16) Answer {
+    double value;
+    unsigned long long seq;
+};
+
+__device__ __forceinline__ unsigned int load_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// A request value read past any cache: the host rewrites these each call.
+__device__ __forceinline__ double load_fresh(const double* p) {
+    double v;
+    asm volatile("ld.global.cv.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__host__ __device__ inline int engine_smem(int slots, int F, int record) {
+    return 128 + kTreeBlock * record + align128(slots * kEngineRows * 4) + align128(kEngineRows * F * 8) +
+           kTreeBlock * kEngineRows * 8;
+}
+
+// The split decided on the double for a float64 model whose keys tied (the
+// rows sit in shared memory: `xs` [row][F]).
+__device__ __forceinline__ bool exact_split(const ForestArgs& a, const double* xs, int row, int node) {
+    const int feat = __ldg(a.feature + node);
+    const double t = __ldg(a.threshold + node);
+    const double mean = a.standardize ? __ldg(a.pre_mean + feat) : 0.0;
+    const double scale = a.standardize ? __ldg(a.pre_scale + feat) : 1.0;
+    const double v = finish(a, xs[row * a.F + feat], mean, scale);
+    return a.le ? (v > t) : !(v < t);
+}
+
+// Device-memory side of a request: the rows CTA 0 copied from the mailbox,
+// and the words it publishes them with.
+struct Relay {
+    unsigned int go;    // number of the request whose rows are in `x`
+    int rows;           // its rows
+    int count;          // CTAs done with the current request
+    int quit;           // 1: every CTA leaves
+};
+
+__device__ __forceinline__ unsigned int load_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void store_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int D, bool LEAF32>
+__global__ void __launch_bounds__(kEngineThreads, 1)
+    engine_kernel(const ForestArgs a, const HeapArgs h, Mailbox* box, const double* x, double* out, double* bpart,
+                  double* xd, Relay* relay, unsigned int first) {
+    Answer* answers = reinterpret_cast<Answer*>(out);
+    constexpr int kRec = heap_record_size(D, LEAF32);
+    constexpr int kSplits = (1 << D) - 1;
+    extern __shared__ __align__(128) unsigned char smem[];
+    volatile unsigned int* ctl = reinterpret_cast<volatile unsigned int*>(smem);  // request, exit/last, rows
+    unsigned char* trees = smem + 128;
+    int* keys = reinterpret_cast<int*>(trees + kTreeBlock * kRec);  // [slot][kEngineRows]
+    double* xs = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(keys) +
+                                           align128(a.slots * kEngineRows * 4));  // [row][F]
+    double* leafv = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(xs) +
+                                              align128(kEngineRows * a.F * 8));   // [tree][row]
+
+    const int tid = threadIdx.x;
+    const int blocks = gridDim.x, block = blockIdx.x;
+    const int t0 = block * kTreeBlock;
+    const int nt = min(kTreeBlock, a.T - t0);
+    const uint32_t mask = (1u << h.slot_bits) - 1u;
+    volatile int* quit = &relay->quit;
+
+    // The block's tree records, once for the engine's life.
+    {
+        const int4* src = reinterpret_cast<const int4*>(h.trees + static_cast<size_t>(t0) * kRec);
+        int4* dst = reinterpret_cast<int4*>(trees);
+        for (int i = tid; i < nt * kRec / 16; i += kEngineThreads) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+
+    unsigned int mine = first;
+    for (;;) {
+        if (tid == 0) {
+            // CTA 0 waits on the mailbox in host memory (the only poller of
+            // the bus), the others on CTA 0's relay in device memory; every
+            // wait is bounded.
+            unsigned int cmd = 0, seq = mine;
+            const unsigned long long since = global_ns();
+            for (long long polls = 0;; ++polls) {
+                seq = block == 0 ? load_acquire_sys(&box->seq) : load_acquire_gpu(&relay->go);
+                if (seq != mine) break;
+                if (*quit || polls >= kEnginePolls || (block == 0 && load_acquire_sys(&box->stop))) {
+                    cmd = 1;
+                    break;
+                }
+                // CTA 0 decides when the engine has idled long enough and
+                // tells the others; they also leave on their own after
+                // twice that.
+                if (global_ns() - since > (block == 0 ? 1u : 2u) * kEngineIdleNs) {
+                    cmd = 1;
+                    break;
+                }
+                __nanosleep(block == 0 ? 32 : 16);
+            }
+            if (cmd && block == 0) atomicExch(&relay->quit, 1);
+            ctl[0] = seq;
+            ctl[1] = cmd;
+            ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, block == 0
+                                                                         ? *reinterpret_cast<volatile int*>(&box->rows)
+                                                                         : *reinterpret_cast<volatile int*>(&relay->rows))));
+        }
+        __syncthreads();
+        if (ctl[1]) return;
+        const unsigned int seq = ctl[0];
+        const int rows = static_cast<int>(ctl[2]);
+        const int values = rows * a.F;
+        if (block == 0) {
+            // Rows from host memory in 16-byte reads, relayed through device
+            // memory to the other CTAs.
+            const int pairs = (values + 1) / 2;
+            for (int i = tid; i < pairs; i += kEngineThreads) {
+                double2 v;
+                asm volatile("ld.global.cv.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(x + 2 * i) : "memory");
+                xs[2 * i] = v.x;
+                xd[2 * i] = v.x;
+                if (2 * i + 1 < values) {
+                    xs[2 * i + 1] = v.y;
+                    xd[2 * i + 1] = v.y;
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {
+                relay->rows = rows;
+                __threadfence();
+                store_release_gpu(&relay->go, seq);
+            }
+        } else {
+            for (int i = tid; i < values; i += kEngineThreads) xs[i] = __ldcg(xd + i);
+            __syncthreads();
+        }
+        for (int i = tid; i < values; i += kEngineThreads) {
+            const int f = i % a.F;
+            const double mean = a.standardize ? __ldg(a.pre_mean + f) : 0.0;
+            const double scale = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
+            put_keys<kEngineRows>(a, keys + i / a.F, __ldg(a.slot_of + f), finish(a, xs[i], mean, scale),
+                                  static_cast<int>(mask));
+        }
+        if (tid < kEngineRows) keys[a.pad_slot * kEngineRows + tid] = INT_MIN;
+        __syncthreads();
+
+        // Thread (pair, local) walks tree t0 + local for rows pair and pair + 4.
+        const int local = tid % kTreeBlock, pair = tid / kTreeBlock;
+        if (local < nt && pair < rows) {
+            const uint32_t base = smem_u32(trees + local * kRec);
+            // Heap index of the leaf row r reaches; `exact` decides tied
+            // splits on the double, `tie` reports whether any split tied.
+            auto walk = [&](int r, bool exact, bool& tie) {
+                const uint32_t col = smem_u32(keys + r);
+                uint32_t i = 0;
+#pragma unroll
+                for (int d = 0; d < D; ++d) {
+                    const uint32_t n = lds_u32(base + 4 * i);
+                    const int k = lds_s32(col + (n & mask) * (kEngineRows * 4));
+                    bool right = k > static_cast<int>(n);
+                    if (k == static_cast<int>(n)) {
+                        tie = true;
+                        if (exact) {
+                            const int node = __ldg(h.node_ids + static_cast<size_t>(t0 + local) * kSplits + i);
+                            if (node >= 0) right = exact_split(a, xs, r, node);
+                        }
+                    }
+                    i = 2 * i + (right ? 2u : 1u);
+                }
+                return i;
+            };
+            for (int r = pair; r < rows; r += kEnginePairs) {
+                bool tie = false;
+                uint32_t i = walk(r, false, tie);
+                if (tie) i = walk(r, true, tie);
+                const uint32_t leaf = i - kSplits;  // leaves follow the 2^D split words
+                leafv[local * kEngineRows + r] = lds_leaf(base + (4u << D) + leaf * (LEAF32 ? 4u : 8u), LEAF32);
+            }
+        }
+        __syncthreads();
+        if (tid < rows) {
+            double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+            for (int j = 0; j < nt; ++j) acc = __dadd_rn(acc, leafv[j * kEngineRows + tid]);
+            __stcg(bpart + static_cast<size_t>(block) * kEngineRows + tid, acc);
+            __threadfence();
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const bool last = atomicAdd(&relay->count, 1) == blocks - 1;
+            if (last) relay->count = 0;  // every CTA has counted this request
+            ctl[1] = last;
+        }
+        __syncthreads();
+        if (ctl[1]) {
+            if (tid < rows) {
+                double v[1] = {__ldcg(bpart + tid)};
+                for (int b = 1; b < blocks; ++b) v[0] = __dadd_rn(v[0], __ldcg(bpart + static_cast<size_t>(b) * kEngineRows + tid));
+                if (a.mean) {
+                    const int n = __ldg(a.counts);
+                    v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
+                }
+                apply_link<1>(a, v, 1);
+                const unsigned long long tag = seq;
+                asm volatile("st.global.v2.b64 [%0], {%1, %2};" ::"l"(answers + tid),
+                             "l"(__double_as_longlong(v[0])), "l"(tag)
+                             : "memory");
+            }
+        }
+        mine = seq;
+        __syncthreads();  // every thread has read this request's control words before thread 0 rewrites them
+    }
+}
+
+template <int D, bool LEAF32>
+void* engine_of() {
+    return reinterpret_cast<void*>(&engine_kernel<D, LEAF32>);
+}
+
+void* pick_engine(int depth, bool leaf32) {
+    switch (depth) {
+        case 1: return leaf32 ? engine_of<1, true>() : engine_of<1, false>();
+        case 2: return leaf32 ? engine_of<2, true>() : engine_of<2, false>();
+        case 3: return leaf32 ? engine_of<3, true>() : engine_of<3, false>();
+        case 4: return leaf32 ? engine_of<4, true>() : engine_of<4, false>();
+        case 5: return leaf32 ? engine_of<5, true>() : engine_of<5, false>();
+        case 6: return leaf32 ? engine_of<6, true>() : engine_of<6, false>();
+        case 7: return leaf32 ? engine_of<7, true>() : engine_of<7, false>();
+        case 8: return leaf32 ? engine_of<8, true>() : engine_of<8, false>();
+    }
+    return nullptr;
+}
+
+bool checked(cudaError_t e, const char* what, std::string& err) {
+    if (e == cudaSuccess) return true;
+    err = std::string(what) + " failed: " + cudaGetErrorString(e);
+    cudaGetLastError();
+    return false;
+}
+
+long long now_ns() {
+    return std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+}  // namespace
+
+struct LatencyEngine {
+    unsigned long long forest = 0;
+    int device = 0;
+    int blocks = 0, F = 0, K = 0;
+    cudaStream_t stream = nullptr;
+    unsigned char* host = nullptr;  // mailbox, then kEngineRows * F inputs, then kEngineRows * K outputs
+    unsigned char* mapped = nullptr;
+    void* dev = nullptr;            // block sums, relayed rows, then the Relay words
+    unsigned int seq = 0;
+    bool launched = false;
+
+    Mailbox* box() const { return reinterpret_cast<Mailbox*>(host); }
+    double* x_host() const { return reinterpret_cast<double*>(host + 64); }
+    Answer* out_host() const { return reinterpret_cast<Answer*>(host + 64 + kEngineRows * F * 8); }
+
+    ~LatencyEngine() {
+        if (host) {
+            reinterpret_cast<volatile unsigned int*>(&box()->stop)[0] = 1;
+            if (stream) cudaStreamSynchronize(stream);  // the engine sees `stop` at its next poll
+        }
+        if (stream) cudaStreamDestroy(stream);
+        if (dev) cudaFree(dev);
+        if (host) cudaFreeHost(host);
+    }
+};
+
+void destroy_engine(LatencyEngine* e) { delete e; }
+
+bool engine_fits(const DevForest& f, long long batch) {
+    if (f.heap.depth <= 0 || batch < 1 || batch > kEngineRows || f.args.K != 1) return false;
+    const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
+    const int smem = engine_smem(f.args.slots, f.args.F, heap_record_bytes(f.heap.depth, f.heap.leaf32));
+    return blocks <= f.sm_count && smem <= 227 * 1024;
+}
+
+// Starts (or restarts) the engine of `e` for forest `f`; `first` is the
+// request number the engine treats as already answered.
+static bool engine_launch(const DevForest& f, LatencyEngine& e, unsigned int first, std::string& err) {
+    void* k = pick_engine(f.heap.depth, f.heap.leaf32 != 0);
+    const int smem = engine_smem(f.args.slots, f.args.F, heap_record_bytes(f.heap.depth, f.heap.leaf32));
+    if (!k || !checked(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                       "cudaFuncSetAttribute", err)) {
+        if (!k) err = "no latency engine for this model";
+        return false;
+    }
+    double* bpart = static_cast<double*>(e.dev);
+    double* xd = bpart + static_cast<size_t>(e.blocks) * kEngineRows;
+    Relay* relay = reinterpret_cast<Relay*>(xd + static_cast<size_t>(kEngineRows) * e.F);
+    // The relay starts at the request the engine treats as answered.
+    const Relay start{first, 0, 0, 0};
+    if (!checked(cudaMemcpyAsync(relay, &start, sizeof start, cudaMemcpyHostToDevice, e.stream), "cudaMemcpyAsync",
+                 err) ||
+        !checked(cudaStreamSynchronize(e.stream), "cudaStreamSynchronize", err)) {
+        return false;
+    }
+    e.box()->stop = 0;
+    Mailbox* box = reinterpret_cast<Mailbox*>(e.mapped);
+    const double* x = reinterpret_cast<const double*>(e.mapped + 64);
+    double* out = reinterpret_cast<double*>(e.mapped + 64 + kEngineRows * e.F * 8);
+    ForestArgs a = f.args;
+    HeapArgs h = f.heap;
+    void* args[] = {&a, &h, &box, &x, &out, &bpart, &xd, &relay, &first};
+    if (!checked(cudaLaunchCooperativeKernel(k, e.blocks, kEngineThreads, args, smem, e.stream),
+                 "latency engine launch", err)) {
+        return false;
+    }
+    e.launched = true;
+    return true;
+}
+
+int engine_predict(const DevForest& f, LatencyEngine*& slot, int dtype, const void* x, size_t batch, double* out,
+                   std::string& err) {
+    if (!engine_fits(f, static_cast<long long>(batch))) return -1;
+    if (slot && slot->forest != f.uid) {
+        delete slot;  // one engine per thread and device: the newest model wins
+        slot = nullptr;
+    }
+    if (!slot) {
+        auto e = std::make_unique<LatencyEngine>();
+        e->forest = f.uid;
+        e->device = f.device;
+        e->blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
+        e->F = f.args.F;
+        e->K = f.args.K;
+        const size_t bytes = 64 + static_cast<size_t>(kEngineRows) * (e->F * 8 + e->K * sizeof(Answer));
+        void* host = nullptr;
+        if (!checked(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "cudaStreamCreate", err) ||
+            !checked(cudaHostAlloc(&host, bytes, cudaHostAllocMapped), "cudaHostAlloc", err)) {
+            return kEngineFailed;
+        }
+        e->host = static_cast<unsigned char*>(host);
+        std::memset(e->host, 0, bytes);
+        void* mapped = nullptr;
+        if (!checked(cudaHostGetDevicePointer(&mapped, host, 0), "cudaHostGetDevicePointer", err) ||
+            !checked(cudaMalloc(&e->dev, (static_cast<size_t>(e->blocks) + e->F) * kEngineRows * 8 + sizeof(Relay)),
+                     "cudaMalloc", err)) {
+            return kEngineFailed;
+        }
+        e->mapped = static_cast<unsigned char*>(mapped);
+        slot = e.release();
+    }
+    LatencyEngine& e = *slot;
+    const bool running = e.launched && cudaStreamQuery(e.stream) == cudaErrorNotReady;
+    cudaGetLastError();
+    if (!running) {
+        if (e.launched && !checked(cudaStreamSynchronize(e.stream), "latency engine", err)) return kEngineFailed;
+        if (!engine_launch(f, e, e.seq, err)) return -1;  // e.g. not enough SMs free: take the graph path
+    }
+    // Post the request: rows first, then its number (x86 keeps the stores in
+    // order, and the engine reads the number with acquire semantics).
+    double* xh = e.x_host();
+    const size_t values = batch * static_cast<size_t>(e.F);
+    if (dtype == 1) {
+        for (size_t i = 0; i < values; ++i) xh[i] = static_cast<const float*>(x)[i];
+    } else {
+        std::memcpy(xh, x, values * sizeof(double));
+    }
+    volatile Mailbox* box = e.box();
+    box->rows = static_cast<int>(batch);
+    const unsigned int seq = ++e.seq;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    box->seq = seq;
+    const long long posted = now_ns();
+    long long checked_at = posted + kEngineCheckNs;
+    volatile Answer* answers = e.out_host();
+    auto answered = [&] {
+        for (size_t r = 0; r < batch; ++r) {
+            if (answers[r].seq != seq) return false;
+        }
+        return true;
+    };
+    for (unsigned spins = 0; !answered(); ++spins) {
+        if ((spins & 1023u) != 1023u) continue;
+        const long long t = now_ns();
+        if (t > posted + kEngineTimeoutNs) {
+            box->stop = 1;
+            err = "the latency engine did not answer within 2 s";
+            return kEngineFailed;
+        }
+        if (t > checked_at) {
+            checked_at = t + kEngineCheckNs;
+            // An engine that left (idle, or racing this request) is restarted;
+            // the request stays posted and is answered by the new one.
+            if (cudaStreamQuery(e.stream) != cudaErrorNotReady) {
+                cudaGetLastError();
+                if (!checked(cudaStreamSynchronize(e.stream), "latency engine", err) ||
+                    !engine_launch(f, e, seq - 1, err)) {
+                    return kEngineFailed;
+                }
+            }
+        }
+        std::this_thread::yield();
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    for (size_t r = 0; r < batch; ++r) out[r] = answers[r].value;
+    return 0;
+}
+
+}  // namespace mlk::cuda

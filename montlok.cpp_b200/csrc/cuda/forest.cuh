@@ -61,6 +61,12 @@ struct SparseArgs {
     const int2* slot_of;         // [F]: slot of (feature, NaN missing), (feature, NaN or zero missing)
 };
 
+// Bytes of one complete-tree record of depth `depth`: 2^depth split words of
+// 4 bytes (the last unused), then 2^depth leaf values, 16-byte aligned.
+__host__ __device__ constexpr int heap_record_size(int depth, bool leaf32) {
+    return ((4 << depth) + (1 << depth) * (leaf32 ? 4 : 8) + 15) & ~15;
+}
+
 // Deep-tree layout (deep_kernels.cu); nodes null when the model has none.
 inline constexpr int kTreeBlock = 64;  // trees per partial sum (the reference sums in 64-tree blocks)
 
@@ -94,7 +100,7 @@ struct DevForest {
 // launches use (they leave it zero); without it the small-batch kernel's
 // counters live in `scratch` and are cleared on the stream first. Returns
 // false with `err` set.
-inline constexpr int kLatencyCounters = 2;
+inline constexpr int kLatencyCounters = 8;
 bool launch_forest(const DevForest& f, int dtype, const void* x, long long batch, double* out, int* leaves,
                    cudaStream_t stream, std::string& err, int* scratch, int* counters = nullptr);
 

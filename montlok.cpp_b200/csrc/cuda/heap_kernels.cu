@@ -61,9 +61,7 @@ constexpr int kHeapSmemLimit = 227 * 1024;
 constexpr int kMaxSlotBits = 10;
 static_assert(kTreeBlock % kTrees == 0, "chunks never straddle a block of 64 trees");
 
-__host__ __device__ constexpr int record_bytes(int depth, bool leaf32) {
-    return ((4 << depth) + (1 << depth) * (leaf32 ? 4 : 8) + 15) & ~15;
-}
+__host__ __device__ constexpr int record_bytes(int depth, bool leaf32) { return heap_record_size(depth, leaf32); }
 
 // Shared memory layout (byte offsets): header (mbarriers [team][2] at 0,
 // buffer-done counters [team][2] at 64, fills issued [team][2] at 96, abort
@@ -342,77 +340,95 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
 // ---------------------------------------------------------------------------
 // Tree-parallel kernel for small batches (at most kLatencyRows rows), where
 // the row-streaming kernel would give one CTA the whole ensemble. CTA
-// (b, g) takes the 64-tree block b for the 32 rows of group g: it bulk-copies
-// the block's trees into shared memory while its threads build the rows' key
-// tables (each thread a few (row, feature) values, all loads in flight at
-// once, the table stride padded to 33 so these scattered writes spread over
-// the banks), its 16 warps walk 4 trees each (lane = row), and 32 threads
-// add the block's 64 leaf values per row in tree order (block 0 onto the
-// base score) into `bpart` ([block][kLatencyRows]). The last CTA of the row
-// group to finish (a device-scope counter, no waiting) adds the block sums
-// in block order and applies the link: the reference's association
-// (trees.cpp:303-388). `count` ([row groups]) starts at zero and the last CTA
-// of each group sets it back to zero.
+// (b, g) takes the 64-tree block b for the (at most) 8 rows of group g, so a
+// one-row call of 1000 trees runs 16 CTAs and a 64-row call 128. It builds
+// the group's key tables in shared memory (every load of a round in flight
+// at once), then each thread walks one tree of the block for two rows
+// (lane = tree), reading the split words straight from the L2-resident tree
+// records: a small call pays no copy of the trees into shared memory, only
+// the dependent loads of its walks, two chains per thread. Leaf values meet
+// in shared memory, where one thread per row adds the block's 64 leaves in
+// tree order (block 0 onto the base score) into `bpart`
+// ([block][kLatencyRows]). The last CTA of the row group to finish (a
+// device-scope counter, no waiting) adds the block sums in block order and
+// applies the link: the reference's association (trees.cpp:303-388).
+// `count` ([row groups]) starts at zero and that last CTA sets it back to
+// zero.
 // ---------------------------------------------------------------------------
 constexpr int kLatencyRows = 64;
-constexpr int kLatencyStride = 33;                  // key table row stride (32 rows + 1)
-constexpr int kLatencyWarps = kTreeBlock / kTrees;  // 16: one per 4 trees of the block
-constexpr int kLatencyThreads = 32 * kLatencyWarps;
-constexpr int kSumBatch = 16;                       // final sum: global loads in flight per thread
+constexpr int kGroupRows = 8;                              // rows per CTA
+constexpr int kLatencyThreads = 256;                       // 64 trees x 4 row pairs
+constexpr int kRowPairs = kLatencyThreads / kTreeBlock;    // 4: thread walks rows p and p + 4
+constexpr int kSumBatch = 16;                              // final sum: global loads in flight per thread
+static_assert(kGroupRows == 2 * kRowPairs, "each thread walks two rows");
+static_assert(kLatencyRows / kGroupRows <= kLatencyCounters, "one counter per row group");
 
 __host__ __device__ inline int latency_smem(int slots, int depth, bool leaf32) {
-    return 128 + align128(slots * kLatencyStride * 4) + align128(kTreeBlock * record_bytes(depth, leaf32)) +
-           kTreeBlock * 32 * 8;
+    return 128 + align128(slots * kGroupRows * 4) + kTreeBlock * kGroupRows * 8;
+}
+
+// One split word of tree record `rec` (global memory, read through L1).
+__device__ __forceinline__ uint32_t split_word(const unsigned char* rec, uint32_t i) {
+    return __ldg(reinterpret_cast<const uint32_t*>(rec) + i);
+}
+
+// Heap index of the leaf tree `tree` (record `rec`) reaches for the row whose
+// key column is `col` ([slot][kGroupRows]); ties of the packed compare are
+// decided on the double (exact_right), as in walk_exact.
+template <int D, typename XT>
+__device__ __forceinline__ uint32_t walk_global(const ForestArgs& a, const HeapArgs& h, const unsigned char* rec,
+                                                const int* col, uint32_t mask, int tree, const XT* x, long long row,
+                                                long long batch, bool exact) {
+    constexpr int kSplits = (1 << D) - 1;
+    uint32_t i = 0;
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+        const uint32_t n = split_word(rec, i);
+        const int k = col[(n & mask) * kGroupRows];
+        bool right = k > static_cast<int>(n);
+        if (exact && k == static_cast<int>(n)) {
+            const int node = __ldg(h.node_ids + static_cast<size_t>(tree) * kSplits + i);
+            if (node >= 0) right = exact_right(a, x, row, batch, node);
+        }
+        i = 2 * i + (right ? 2u : 1u);
+    }
+    return i;
 }
 
 template <int D, bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const ForestArgs a, const HeapArgs h,
-                                                                    const XT* __restrict__ x, long long batch,
-                                                                    double* __restrict__ out, double* bpart,
-                                                                    int* count) {
+__global__ void __launch_bounds__(kLatencyThreads) latency_kernel(const ForestArgs a, const HeapArgs h,
+                                                                  const XT* __restrict__ x, long long batch,
+                                                                  double* __restrict__ out, double* bpart, int* count) {
     constexpr int kRec = record_bytes(D, LEAF32);
+    constexpr int kSplits = (1 << D) - 1;
     constexpr int kPerThread = 8;  // values one thread loads per round of the prepare
     extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-    int* flag = reinterpret_cast<int*>(smem + 64);
-    int* keys = reinterpret_cast<int*>(smem + 128);
-    unsigned char* trees = smem + 128 + align128(a.slots * kLatencyStride * 4);
-    double* leafv = reinterpret_cast<double*>(trees + align128(kTreeBlock * kRec));  // [tree][32 rows]
+    int* flag = reinterpret_cast<int*>(smem);
+    int* keys = reinterpret_cast<int*>(smem + 128);  // [slot][kGroupRows]
+    double* leafv = reinterpret_cast<double*>(smem + 128 + align128(a.slots * kGroupRows * 4));  // [tree][row]
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
     const int block = blockIdx.x % blocks, group = blockIdx.x / blocks;
-    const long long row0 = 32ll * group;
+    const long long row0 = static_cast<long long>(kGroupRows) * group;
+    const int rows = static_cast<int>(min(static_cast<long long>(kGroupRows), batch - row0));
     const int t0 = block * kTreeBlock;
     const int nt = min(kTreeBlock, a.T - t0);
-    // Device records are padded to whole chunks of kTrees trees.
-    const int copied = min(kTreeBlock, (a.T + kTrees - 1) / kTrees * kTrees - t0);
     const uint32_t mask = (1u << h.slot_bits) - 1u;
 
-    if (tid == 0) {
-        mbar_init(bar);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    if (tid == 0 && !a.skip_copies) {
-        bulk_load(smem_u32(trees), h.trees + static_cast<size_t>(t0) * kRec, static_cast<uint32_t>(copied * kRec), bar);
-    }
-    // Keys of the group's live rows: value i is (row row0 + i / F, feature
-    // i % F). Padding rows keep whatever the table holds: their walks read
-    // only in-bounds shared memory (slots come from the split words) and
-    // their leaves are never added.
-    const int values = static_cast<int>(min(32ll, batch - row0)) * a.F;
+    // Keys of the group's rows: value i is (row row0 + i / F, feature i % F);
+    // rows past the batch keep whatever the table holds (their walks read
+    // in-bounds shared memory; their leaves are never added).
+    const int values = rows * a.F;
     for (int i0 = tid; i0 < values; i0 += kPerThread * kLatencyThreads) {
-        // Every load of the round first (value, slots, preprocess), then the keys.
         double v[kPerThread], mean[kPerThread], scale[kPerThread];
         int4 slot[kPerThread];
 #pragma unroll
         for (int j = 0; j < kPerThread; ++j) {
             const int i = i0 + j * kLatencyThreads;
             const int f = i % a.F;
-            const long long row = row0 + i / a.F;
             const bool live = i < values;
-            v[j] = live ? load_x(x + row * a.F + f) : 0.0;
+            v[j] = live ? load_x(x + (row0 + i / a.F) * a.F + f) : 0.0;
             slot[j] = live ? __ldg(a.slot_of + f) : make_int4(-1, -1, -1, -1);
             mean[j] = (live && a.standardize) ? __ldg(a.pre_mean + f) : 0.0;
             scale[j] = (live && a.standardize) ? __ldg(a.pre_scale + f) : 1.0;
@@ -421,44 +437,62 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
         for (int j = 0; j < kPerThread; ++j) {
             const int i = i0 + j * kLatencyThreads;
             if (i < values) {
-                put_keys<kLatencyStride>(a, keys + i / a.F, slot[j], finish(a, v[j], mean[j], scale[j]),
-                                         static_cast<int>(mask));
+                put_keys<kGroupRows>(a, keys + i / a.F, slot[j], finish(a, v[j], mean[j], scale[j]),
+                                     static_cast<int>(mask));
             }
         }
     }
-    if (tid < 32) keys[a.pad_slot * kLatencyStride + tid] = INT_MIN;
+    if (tid < kGroupRows) keys[a.pad_slot * kGroupRows + tid] = INT_MIN;
     __syncthreads();
-    const bool arrived = __syncthreads_and(mbar_wait(bar, 0u, a.wait_ns));
-    if (!arrived && tid == 0) {
-        // The block's trees never arrived: record the failure for the host
-        // (this call's results are void) and leave no copy in flight into
-        // shared memory (a second bounded wait for an issued one). The CTA
-        // still counts itself below, so the row group's counter returns to
-        // zero for the next launch.
-        atomicExch(a.status, 1);
-        if (!a.skip_copies) mbar_wait(bar, 0u, a.wait_ns);
-    }
-    const long long row = row0 + lane;
-    if (arrived && warp * kTrees < copied) {
-        double v[kTrees];
-        walk_leaves<D, kLatencyStride, LEAF32>(a, h, smem_u32(trees) + warp * kTrees * kRec,
-                                               smem_u32(keys) + lane * 4, mask, t0 + warp * kTrees, x, row, batch, v);
+
+    // Walks: thread (pair, lane) takes tree t0 + tid % 64 for rows pair and
+    // pair + 4 of the group, two independent chains of dependent loads.
+    const int local = tid % kTreeBlock, pair = tid / kTreeBlock;
+    const int tree = t0 + local;
+    if (local < nt && pair < rows) {
+        const unsigned char* rec = h.trees + static_cast<size_t>(tree) * kRec;
+        const int ra = pair, rb = pair + kRowPairs;
+        const bool two = rb < rows;
+        const int* ca = keys + ra;
+        const int* cb = keys + rb;
+        uint32_t ia = 0, ib = 0;
+        bool tie = false;
 #pragma unroll
-        for (int t = 0; t < kTrees; ++t) leafv[(warp * kTrees + t) * 32 + lane] = v[t];
+        for (int d = 0; d < D; ++d) {
+            const uint32_t na = split_word(rec, ia);
+            const uint32_t nb = split_word(rec, ib);
+            const int ka = ca[(na & mask) * kGroupRows];
+            const int kb = cb[(nb & mask) * kGroupRows];
+            tie |= ka == static_cast<int>(na) || (two && kb == static_cast<int>(nb));
+            ia = 2 * ia + (ka > static_cast<int>(na) ? 2u : 1u);
+            ib = 2 * ib + (kb > static_cast<int>(nb) ? 2u : 1u);
+        }
+        if (tie) {
+            ia = walk_global<D>(a, h, rec, ca, mask, tree, x, row0 + ra, batch, true);
+            if (two) ib = walk_global<D>(a, h, rec, cb, mask, tree, x, row0 + rb, batch, true);
+        }
+        auto leaf = [&](uint32_t i) {
+            const unsigned char* at = rec + (4 << D);
+            const uint32_t l = i - kSplits;
+            return LEAF32 ? static_cast<double>(__ldg(reinterpret_cast<const float*>(at) + l))
+                          : __ldg(reinterpret_cast<const double*>(at) + l);
+        };
+        leafv[local * kGroupRows + ra] = leaf(ia);
+        if (two) leafv[local * kGroupRows + rb] = leaf(ib);
     }
     __syncthreads();
-    if (arrived && tid < 32 && row < batch) {
+    if (tid < rows) {
         double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
-        for (int t0 = 0; t0 < nt; t0 += 8) {
+        for (int j0 = 0; j0 < nt; j0 += 8) {
             double v[8];  // the loads together, the adds in order
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = t0 + j < nt ? leafv[(t0 + j) * 32 + tid] : 0.0;
+            for (int j = 0; j < 8; ++j) v[j] = j0 + j < nt ? leafv[(j0 + j) * kGroupRows + tid] : 0.0;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                if (t0 + j < nt) acc = __dadd_rn(acc, v[j]);
+                if (j0 + j < nt) acc = __dadd_rn(acc, v[j]);
             }
         }
-        __stcg(bpart + static_cast<size_t>(block) * kLatencyRows + row, acc);
+        __stcg(bpart + static_cast<size_t>(block) * kLatencyRows + row0 + tid, acc);
         __threadfence();
     }
     __syncthreads();
@@ -467,8 +501,9 @@ __global__ void __launch_bounds__(kLatencyThreads, 1) latency_kernel(const Fores
         if (*flag) count[group] = 0;  // every CTA of the group has counted: ready for the next launch
     }
     __syncthreads();
-    if (!*flag || tid >= 32 || row >= batch) return;
+    if (!*flag || tid >= rows) return;
     // Last CTA of the row group: the block sums in order, then mean and link.
+    const long long row = row0 + tid;
     double v[1] = {__ldcg(bpart + row)};
     for (int b0 = 1; b0 < blocks; b0 += kSumBatch) {
         double p[kSumBatch];
@@ -620,7 +655,7 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
 size_t latency_scratch_bytes(const DevForest& f) {
     if (f.heap.depth <= 0) return 0;
     const size_t blocks = static_cast<size_t>((f.args.T + kTreeBlock - 1) / kTreeBlock);
-    return blocks * kLatencyRows * sizeof(double) + 2 * sizeof(int);
+    return blocks * kLatencyRows * sizeof(double) + kLatencyCounters * sizeof(int);
 }
 
 // The tree-parallel kernel takes batches of at most kLatencyRows rows when
@@ -654,7 +689,7 @@ bool launch_latency(const DevForest& f, int dtype, const void* x, long long batc
         }
     }
     const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
-    const int groups = static_cast<int>((batch + 31) / 32);
+    const int groups = static_cast<int>((batch + kGroupRows - 1) / kGroupRows);
     double* bpart = static_cast<double*>(scratch);
     // The kernel leaves its counters at zero: a dedicated zeroed buffer needs
     // no clearing, counters in the shared scratch do.

@@ -52,6 +52,11 @@ enum { MLK_PTR_PAGEABLE = 0, MLK_PTR_PINNED = 1, MLK_PTR_DEVICE = 2 };
 int mlk_cuda_device_count(int* count, char* err, size_t errlen);
 /* Host threads that copy pageable inputs into pinned staging. */
 void mlk_cuda_set_copy_threads(int threads);
+/* Nonzero: host-buffer predicts of at most 8 rows on complete-tree models are
+ * answered by a resident kernel of the calling thread (engine_kernels.cu),
+ * started on first use; zero: they replay a cached graph, and a thread's
+ * engine is released at its next call. */
+void mlk_cuda_set_latency_engine(int on);
 int mlk_cuda_current_device(int* device, char* err, size_t errlen);
 int mlk_cuda_pointer_kind(const void* p, int* kind, int* device);
 

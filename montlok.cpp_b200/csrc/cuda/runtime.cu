@@ -36,6 +36,7 @@
 #include <vector>
 
 #include "async_copy.cuh"
+#include "engine.cuh"
 #include "forest.cuh"
 #include "mlk_cuda.h"
 
@@ -47,6 +48,7 @@ constexpr int kInvalid = 1;
 constexpr size_t kChunkBytes = size_t{64} << 20;  // input bytes per pipelined chunk
 
 std::atomic<int> g_copy_threads{0};  // 0: every hardware thread
+std::atomic<int> g_latency_engine{0};  // nonzero: small host calls go to the calling thread's latency engine
 
 int copy_threads() {
     const int n = g_copy_threads.load(std::memory_order_relaxed);
@@ -299,7 +301,9 @@ struct Workspace {
     PinnedBuffer hx[2], hout[2];
     std::vector<CachedGraph> graphs;
     unsigned long long tick = 0;
+    LatencyEngine* engine = nullptr;  // this thread's resident small-call kernel, when latency threads are on
     ~Workspace() {
+        destroy_engine(engine);
         for (auto& g : graphs) {
             if (g.exec) cudaGraphExecDestroy(g.exec);
             if (g.graph) cudaGraphDestroy(g.graph);
@@ -340,13 +344,16 @@ constexpr size_t kGraphCache = 8;    // graphs kept per workspace
 // input is pinned already, the graph's copy reads it in place), a cached
 // graph of (host -> device copy, kernel) runs on the workspace's first
 // stream, the kernel storing its results into pinned host memory directly,
-// and the result is copied out. (Letting the small-batch kernel read a few
-// rows over the bus instead of copying them was slower: each of its CTAs
-// pays the bus latency.) The graph is captured on the first call with this
-// forest, input type and row count (or after a staging buffer grew), so
-// later calls of the same shape pay one graph launch instead of separate
-// stream operations and kernel launches.
-int run_small(const DevForest& base, int dtype, const void* x, size_t batch, double* out, char* err,
+// and the result is copied out. (Calls of at most kDirectRows rows could skip
+// the device copy, the kernel reading the staged rows over the bus; measured
+// slower for 1 and 8 rows, 21.5 and 30.6 us against 18.1 and 22.1, since
+// every CTA pays the bus latency, so it is off.) The graph is captured
+// on the first call with this forest, input type and row count (or after a
+// staging buffer grew), so later calls of the same shape pay one graph
+// launch instead of separate stream operations and kernel launches.
+constexpr size_t kDirectRows = 0;  // small-batch calls whose kernel reads the rows from pinned host memory
+
+int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_t batch, double* out, char* err,
               size_t errlen) {
     std::string e;
     DeviceGuard guard(base.device);
@@ -368,6 +375,10 @@ int run_small(const DevForest& base, int dtype, const void* x, size_t batch, dou
         return kInternal;
     }
     cudaStream_t st = w->stream[0];
+    // The fewest rows need no copy at all: the kernel reads them from the
+    // pinned staging buffer over the bus, so the graph is one kernel node.
+    const bool direct = batch <= kDirectRows && latency_fits(f, static_cast<long long>(batch));
+    const void* kernel_x = direct ? w->hx[0].p : w->dx[0].p;
     const void* buffers[5] = {w->dx[0].p, nullptr, w->hx[0].p, w->hout[0].p, scratch ? w->scratch.p : nullptr};
     CachedGraph* g = nullptr;
     for (auto& c : w->graphs) {
@@ -397,14 +408,14 @@ int run_small(const DevForest& base, int dtype, const void* x, size_t batch, dou
     if (!g) {
         bool good = ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture", e);
         if (good) {
-            good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e);
+            good = direct || copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e);
             if (good && injected("launch")) {
                 e = "kernel launch failed: injected fault (MONTLOK_FAULT_INJECT=launch)";
                 good = false;
             }
             // The kernel stores the results straight into the pinned staging
             // buffer (host memory the device addresses directly).
-            good = good && launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
+            good = good && launch_forest(f, dtype, kernel_x, static_cast<long long>(batch),
                                          static_cast<double*>(w->hout[0].p), nullptr, st, e,
                                          static_cast<int*>(w->scratch.p), static_cast<int*>(w->counters.p));
             cudaGraph_t graph = nullptr;
@@ -456,9 +467,7 @@ int run_small(const DevForest& base, int dtype, const void* x, size_t batch, dou
         }
     }
     g->used = ++w->tick;
-    int kind = MLK_PTR_PAGEABLE, dev = -1;
-    mlk_cuda_pointer_kind(x, &kind, &dev);
-    const void* src = (kind == MLK_PTR_PINNED && g->input_copy) ? x : w->hx[0].p;
+    const void* src = (x_kind == MLK_PTR_PINNED && g->input_copy) ? x : w->hx[0].p;
     if (src != g->input) {
         if (!ok(cudaGraphExecMemcpyNodeSetParams1D(g->exec, g->input_copy, w->dx[0].p, src, in_bytes,
                                                    cudaMemcpyHostToDevice),
@@ -514,8 +523,21 @@ int run_host(const DevForest& base, int dtype, const void* x, size_t batch, Out*
     const bool pin_x = kx == MLK_PTR_PINNED, pin_out = ko == MLK_PTR_PINNED;
     const bool dev_x = kx == MLK_PTR_DEVICE, dev_out = ko == MLK_PTR_DEVICE;
     if constexpr (std::is_same_v<Out, double>) {
+        if (!leaves && !dev_x && !dev_out && batch <= static_cast<size_t>(kEngineRows)) {
+            if (g_latency_engine.load(std::memory_order_relaxed) > 0) {
+                const int served = engine_predict(base, w->engine, dtype, x, batch, out, e);
+                if (served == 0) return 0;
+                if (served != -1) {
+                    put_error(err, errlen, e);
+                    return kInternal;
+                }
+            } else if (w->engine) {
+                destroy_engine(w->engine);  // latency threads were turned off: release the SMs
+                w->engine = nullptr;
+            }
+        }
         if (!leaves && batch <= kGraphRows && !dev_x && !dev_out) {
-            return run_small(base, dtype, x, batch, out, err, errlen);
+            return run_small(base, dtype, x, kx, batch, out, err, errlen);
         }
     }
     // A model that casts features to float32 and has no preprocessing uses
@@ -889,6 +911,8 @@ using mlk::cuda::put_error;
 extern "C" {
 
 void mlk_cuda_set_copy_threads(int threads) { mlk::cuda::g_copy_threads.store(std::max(1, threads)); }
+
+void mlk_cuda_set_latency_engine(int on) { mlk::cuda::g_latency_engine.store(on); }
 
 int mlk_cuda_device_count(int* count, char* err, size_t errlen) {
     *count = 0;

@@ -28,6 +28,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "libmontlok_oracle.so"
 REF_LIB = HERE / "_ref" / "libmontlok_ref.so"
+CONSUMER = HERE / "_ref" / "test_core_consumer"  # the reference's C++ test linked to libmontlok.so
 
 
 def reference_sources() -> Path | None:
@@ -54,6 +55,8 @@ def build(reference: bool = True) -> None:
     variables = []
     if reference and REFERENCE_SOURCES is not None:
         targets.append("ref")
+        if (HERE.parent / "montlok.cpp_b200" / "python" / "montlok" / "libmontlok.so").exists():
+            targets.append("consumer")
         variables.append(f"REF={REFERENCE_SOURCES}")
     subprocess.run(["make", "-s", "-C", str(HERE), *variables, *targets], check=True)
 

@@ -147,11 +147,12 @@ SMALL_MODELS = {
 
 
 @pytest.mark.parametrize("name", sorted(SMALL_MODELS))
-@pytest.mark.parametrize("rows", [1, 8, 31, 32, 33, 64])
+@pytest.mark.parametrize("rows", [1, 3, 4, 5, 8, 9, 31, 33, 64])
 def test_small_batches_tree_parallel(gpu, name, rows):
     """Batches of at most 64 rows on complete-tree models take the
-    tree-parallel kernel (one CTA per 32 trees, block sums by the last CTA of
-    each block, the link by the last block)."""
+    tree-parallel kernel (one CTA per 64-tree block and group of 8 rows, each
+    thread one tree for two rows, block sums in tree order, the link by the
+    last CTA of each row group); partial groups and partial blocks."""
     model = SMALL_MODELS[name]()
     m = montlok.load(model)
     rng = np.random.default_rng(rows)
