@@ -473,6 +473,28 @@ def sharded_call(torch, montlok, cfg, world: int, batch: int, steps: int) -> dic
             "h2d_bytes_per_call": batch * model.features * 8, "timing": "host clock around one blocking call"}
 
 
+def h2d_rate(torch, barrier, gib: int = 1) -> float:
+    """Seconds of one pinned host -> device copy of `gib` GiB on this rank's
+    GPU, every rank copying at the same time (the ceiling the e2e figures run
+    against: each GPU's link and the host memory the ranks share)."""
+    src = torch.empty(gib << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(gib << 30, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dst.copy_(src, non_blocking=True)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+    end.record(stream)
+    barrier()
+    seconds = start.elapsed_time(end) / 3e3
+    del src, dst
+    return seconds
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -529,9 +551,11 @@ def main() -> None:
     clock = clocks.stop()
     m.check(host)
 
+    h2d_s = h2d_rate(torch, barrier)
+
     from montlok.distributed import max_over_ranks
 
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], device="cuda")
+    ms, e2e_ms, h2d_s = max_over_ranks([ms, e2e_ms, h2d_s], device="cuda")
 
     line = None
     if rank == 0:
@@ -546,6 +570,9 @@ def main() -> None:
             "roofline": roofline(args.config, ms, batch, m.F),
             "gpu_launches": args.steps * m.launches_per_step(),
             "clocks": clock,
+            "h2d_ceiling": {"per_gpu_gbs": (1 << 30) / h2d_s / 1e9, "all_gpus_gbs": world * (1 << 30) / h2d_s / 1e9,
+                            "e2e_input_gbs": world * batch * m.F * 8 / (e2e_ms / 1e3) / 1e9,
+                            "how": "3 pinned 1 GiB host->device copies per rank, all ranks at once, slowest rank"},
         }
     del m, x
     torch.cuda.empty_cache()

@@ -5,8 +5,11 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <thread>
 
 #include "../cuda/mlk_cuda.h"
@@ -33,6 +36,72 @@ const json::Value& empty_object() {
 void check_cuda(int status, const char* err) {
     if (status != 0) fail(static_cast<Status>(status), err);
 }
+
+// One long-lived host thread per GPU for host-buffer predicts split over
+// devices (set_devices): each keeps its own CUDA workspace (streams, device
+// buffers, pinned staging) from call to call, so a sharded call allocates
+// nothing once every worker has served one call of its size. Calls from
+// several threads queue per device.
+class DeviceWorkers {
+public:
+    static DeviceWorkers& get() {
+        static DeviceWorkers* workers = new DeviceWorkers();  // never destroyed: workers may be busy at exit
+        return *workers;
+    }
+
+    // Runs jobs[d] on device d's worker for every d, and returns when all ran.
+    void run(std::vector<std::function<void()>>& jobs) {
+        struct Pending {
+            std::mutex mu;
+            std::condition_variable cv;
+            size_t left;
+        } pending;
+        pending.left = jobs.size();
+        for (size_t d = 0; d < jobs.size(); ++d) {
+            Worker& w = worker(static_cast<int>(d));
+            std::lock_guard<std::mutex> lock(w.mu);
+            w.queue.push_back([&pending, &jobs, d] {
+                jobs[d]();
+                std::lock_guard<std::mutex> done(pending.mu);
+                if (--pending.left == 0) pending.cv.notify_all();
+            });
+            w.cv.notify_one();
+        }
+        std::unique_lock<std::mutex> lock(pending.mu);
+        pending.cv.wait(lock, [&] { return pending.left == 0; });
+    }
+
+private:
+    struct Worker {
+        std::mutex mu;
+        std::condition_variable cv;
+        std::deque<std::function<void()>> queue;
+    };
+
+    Worker& worker(int device) {
+        std::lock_guard<std::mutex> lock(mu_);
+        while (static_cast<int>(workers_.size()) <= device) {
+            workers_.push_back(std::make_unique<Worker>());
+            Worker* w = workers_.back().get();
+            std::thread([w] {
+                for (;;) {
+                    std::function<void()> job;
+                    {
+                        std::unique_lock<std::mutex> lock(w->mu);
+                        w->cv.wait(lock, [&] { return !w->queue.empty(); });
+                        job = std::move(w->queue.front());
+                        w->queue.pop_front();
+                    }
+                    job();
+                }
+            }).detach();
+        }
+        return *workers_[static_cast<size_t>(device)];
+    }
+
+    std::mutex mu_;
+    std::vector<std::unique_ptr<Worker>> workers_;
+};
 
 }  // namespace
 
@@ -243,11 +312,11 @@ void Model::predict(InputType type, const void* x, size_t batch, double* out) co
     std::vector<std::string> message(static_cast<size_t>(use));
     const char* inject = std::getenv("MONTLOK_FAULT_INJECT");
     const bool fail_shard = inject && std::strcmp(inject, "shard") == 0;
-    std::vector<std::thread> workers;
+    std::vector<std::function<void()>> jobs(static_cast<size_t>(use));
     for (int d = 0; d < use; ++d) {
         const size_t lo = std::min(batch, static_cast<size_t>(d) * per), hi = std::min(batch, lo + per);
-        if (lo >= hi) continue;
-        workers.emplace_back([&, d, lo, hi] {
+        jobs[d] = [&, d, lo, hi] {
+            if (lo >= hi) return;
             char e[kErr] = {0};
             if (fail_shard && d == use - 1) {
                 status[d] = static_cast<int>(Status::Internal);
@@ -257,9 +326,9 @@ void Model::predict(InputType type, const void* x, size_t batch, double* out) co
             status[d] = mlk_cuda_predict_host(replicas[d], dtype, static_cast<const char*>(x) + lo * row_bytes, hi - lo,
                                               out + lo * outputs_, e, sizeof e);
             message[d] = e;
-        });
+        };
     }
-    for (auto& w : workers) w.join();
+    DeviceWorkers::get().run(jobs);
     for (int d = 0; d < use; ++d) {
         if (status[d] != 0) fail(static_cast<Status>(status[d]), "device " + std::to_string(d) + ": " + message[d]);
     }
