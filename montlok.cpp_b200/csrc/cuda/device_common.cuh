@@ -136,9 +136,13 @@ __device__ __forceinline__ void put_made_keys(int* col, int4 s, int k, bool nan,
 // and its key written to every variant slot its feature uses. Rows at or past
 // `batch` are prepared as 0.0: their walks read in-bounds shared memory and
 // their results are never stored.
-template <int STRIDE, typename XT>
-__device__ void prepare_own_row(const ForestArgs& a, const XT* __restrict__ x, long long row, long long batch, int* col,
-                                int f_begin, int f_end, int mask) {
+//
+// prepare_row_with is the same walk over the row with the keys handed to
+// put(feature, key, nan, zero) instead; the loop is warp-uniform when
+// f_begin and f_end are, so put may hold warp-collective instructions.
+template <typename XT, typename Put>
+__device__ __forceinline__ void prepare_row_with(const ForestArgs& a, const XT* __restrict__ x, long long row,
+                                                 long long batch, int f_begin, int f_end, Put&& put) {
     constexpr int kBatch = 8;
     constexpr int kVec = 16 / static_cast<int>(sizeof(XT));  // values per 16-byte load
     const bool live = row < batch;
@@ -183,10 +187,18 @@ __device__ void prepare_own_row(const ForestArgs& a, const XT* __restrict__ x, l
                 int k;
                 bool nan, zero;
                 key_of(a, val, k, nan, zero);
-                put_made_keys<STRIDE>(col, __ldg(a.slot_of + f), k, nan, zero, mask);
+                put(f, k, nan, zero);
             }
         }
     }
+}
+
+template <int STRIDE, typename XT>
+__device__ void prepare_own_row(const ForestArgs& a, const XT* __restrict__ x, long long row, long long batch, int* col,
+                                int f_begin, int f_end, int mask) {
+    prepare_row_with(a, x, row, batch, f_begin, f_end, [&](int f, int k, bool nan, bool zero) {
+        put_made_keys<STRIDE>(col, __ldg(a.slot_of + f), k, nan, zero, mask);
+    });
 }
 
 inline constexpr int kPrepTile = 4;                               // features per transpose tile

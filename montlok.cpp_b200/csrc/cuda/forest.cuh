@@ -129,6 +129,9 @@ bool launch_latency(const DevForest& f, int dtype, const void* x, long long batc
                     std::string& err, void* scratch, int* counters);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err);
+// Whether launch_heap runs the staged variant (keys prepared in TMEM by
+// producer warps while the walkers walk) for `batch` rows.
+bool heap_staged(const DevForest& f, long long batch);
 
 // Deep-tree kernel (one output): whether a model's key tables fit, launch.
 bool deep_fits(int slots);

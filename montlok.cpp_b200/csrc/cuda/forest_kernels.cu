@@ -414,7 +414,10 @@ extern "C" const char* mlk_cuda_kernel_name(const mlk_dev_forest* forest, size_t
     using namespace mlk::cuda;
     const DevForest& f = forest->f;
     const long long rows = static_cast<long long>(batch);
-    if (f.heap.depth > 0) return latency_fits(f, rows) ? "small-batch" : "complete-tree";
+    if (f.heap.depth > 0) {
+        if (latency_fits(f, rows)) return "small-batch";
+        return heap_staged(f, rows) ? "complete-tree-staged" : "complete-tree";
+    }
     if (f.sparse.teams > 0) return "multi-output";
     if (f.deep.records) return "deep-tree";
     return shape_of(f.args).global_keys ? "generic-global-keys" : "generic";

@@ -50,6 +50,7 @@
 #include "async_copy.cuh"
 #include "device_common.cuh"
 #include "forest.cuh"
+#include "tmem.cuh"
 
 namespace mlk::cuda {
 namespace {
@@ -338,6 +339,274 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
 }
 
 // ---------------------------------------------------------------------------
+// Staged complete-tree kernel: heap_kernel's walk with the prepare taken off
+// the walkers' path. Beside the four teams of 128 walker threads (warps
+// 0..15) run four producer warps (16..19), one thread per row of the group:
+// while the walkers walk row group g, the producers read the rows of the
+// CTA's next group and write their keys into tensor memory, lane = row of
+// the group, column = slot (the pad slot, always INT_MIN, is not staged).
+// At the start of a group every walker copies its own row's keys for a
+// quarter of the slots from its TMEM lane (a warp's rows are exactly the 32
+// lanes its quarter of TMEM holds) into the shared key table. Two mbarriers
+// hand the stage over: `full` (one arrival per producer warp: the group's
+// keys are in TMEM) and `empty` (one per walker warp: copied out, the stage
+// may be overwritten). Each is waited on with the time bound and abort flag
+// of the chunk waits; the walkers' round barriers are a named barrier of the
+// 512 walkers, the producers never take part in them. The CTA allocates the
+// stage's TMEM columns once and frees them on every way out, after a last
+// barrier of all 640 threads. Only for 128 rows per CTA and models whose pad
+// slot is at most 512 (the stage fits 512 columns); one CTA per SM (its
+// registers), launched one per SM.
+// ---------------------------------------------------------------------------
+constexpr int kStageRows = 128;
+constexpr int kWalkers = kTeams * kStageRows;  // 512
+constexpr int kProducerWarps = 4;              // one per quarter of TMEM's 128 lanes
+constexpr int kStagedThreads = kWalkers + 32 * kProducerWarps;
+constexpr int kMaxStageCols = 512;
+
+// The walkers' barrier (named barrier 1, the 512 walker threads only);
+// returns whether any walker passed a nonzero `v`.
+__device__ __forceinline__ bool walkers_sync_or(int v) {
+    int any;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.s32 q, %1, 0; bar.red.or.pred p, 1, %2, q; selp.s32 %0, 1, 0, p; }"
+        : "=r"(any)
+        : "r"(v), "n"(kWalkers)
+        : "memory");
+    return any != 0;
+}
+__device__ __forceinline__ void walkers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWalkers) : "memory"); }
+
+// TMEM columns a model's stage takes: the smallest power of two, at least
+// 32, holding slots 0 .. pad_slot - 1; 0 when it needs more than 512.
+__host__ __device__ inline int stage_cols(int pad_slot) {
+    int c = 32;
+    while (c < pad_slot) c *= 2;
+    return c <= kMaxStageCols ? c : 0;
+}
+
+template <int D, bool LEAF32, typename XT>
+__global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const ForestArgs a, const HeapArgs h,
+                                                                        const XT* __restrict__ x, long long batch,
+                                                                        double* __restrict__ out, int cols) {
+    constexpr int R = kStageRows;
+    constexpr int kChunkBytes = kTrees * record_bytes(D, LEAF32);
+    constexpr int kWarpsPerTeam = R / 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const Layout L = layout_of(a.slots, D, LEAF32, R);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                // [team][buffer]
+    unsigned* done = reinterpret_cast<unsigned*>(smem + 64);         // [team][buffer]: warps done, cumulative
+    unsigned* fills = reinterpret_cast<unsigned*>(smem + 96);        // [team][buffer]: copies issued
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + 128);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 136);        // stage written (producer warps)
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + 144);       // stage copied out (walker warps)
+    uint32_t* stage_addr = reinterpret_cast<uint32_t*>(smem + 152);  // TMEM address of the stage
+    int* keys = reinterpret_cast<int*>(smem + L.keys);
+    double* parts = reinterpret_cast<double*>(smem + L.parts);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const long long groups = (batch + R - 1) / R;
+    const size_t row_bytes = static_cast<size_t>(a.F) * sizeof(XT);
+    const uint32_t mask = (1u << h.slot_bits) - 1u;
+    const int staged = a.pad_slot;  // slots 0 .. staged - 1 go through TMEM
+
+    if (tid == 0) {
+        for (int b = 0; b < 2 * kTeams; ++b) {
+            mbar_init(&bar[b]);
+            done[b] = 0u;
+            fills[b] = 0u;
+        }
+        mbar_init(full, kProducerWarps);
+        mbar_init(empty, kWalkers / 32);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (blockIdx.x < groups) {
+            const long long r0 = static_cast<long long>(blockIdx.x) * R;
+            prefetch_l2(x + r0 * a.F, static_cast<size_t>(min(static_cast<long long>(R), batch - r0)) * row_bytes);
+        }
+    }
+    if (warp == kWalkers / 32) tmem_alloc(stage_addr, static_cast<uint32_t>(cols));
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
+    const uint32_t stage = *stage_addr;
+
+    if (tid >= kWalkers) {
+        // Producer: row p of every group this CTA takes, into TMEM lane p.
+        const int p = tid - kWalkers;
+        const uint32_t lane_base = stage + (static_cast<uint32_t>(p & ~31) << 16);
+        int it = 0;
+        for (long long g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+            if (it > 0) {
+                // The walkers have copied the previous group out of the stage.
+                const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(empty, (it - 1) & 1, a.wait_ns, abort));
+                if (!ok) {
+                    if (lane == 0) *abort = 1;
+                    break;
+                }
+                tmem_fence_after_sync();
+            }
+            prepare_row_with(a, x, g * R + p, batch, 0, a.F, [&](int f, int k, bool nan, bool zero) {
+                const int4 s = __ldg(a.slot_of + f);
+                auto tag = [mask](int key, int slot) { return (key & ~static_cast<int>(mask)) | (slot & static_cast<int>(mask)); };
+                if (s.x >= 0) tmem_st1(lane_base + s.x, tag(nan ? INT_MAX : k, s.x));
+                if (s.y >= 0) tmem_st1(lane_base + s.y, tag(nan ? INT_MIN : k, s.y));
+                if (s.z >= 0) tmem_st1(lane_base + s.z, tag(zero ? INT_MAX : k, s.z));
+                if (s.w >= 0) tmem_st1(lane_base + s.w, tag(zero ? INT_MIN : k, s.w));
+            });
+            tmem_wait_st();
+            tmem_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full);
+            if (p == 0 && g + gridDim.x < groups) {  // the rows of the next group this CTA prepares, into L2
+                const long long r1 = (g + gridDim.x) * R;
+                prefetch_l2(x + r1 * a.F, static_cast<size_t>(min(static_cast<long long>(R), batch - r1)) * row_bytes);
+            }
+        }
+    } else {
+        const int team = tid / R, r = tid % R;
+        const bool issuer = r == 0;  // issues the team's first two copies of a row group
+        const int chunks = (a.T + kTrees - 1) / kTrees;
+        const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
+        const int rounds = (blocks + kTeams - 1) / kTeams;
+        int n_team = 0;
+        for (int b = team; b < blocks; b += kTeams) n_team += min(kChunksPerBlock, chunks - b * kChunksPerBlock);
+        auto chunk_at = [&](int q) {
+            return (team + kTeams * (q / kChunksPerBlock)) * kChunksPerBlock + q % kChunksPerBlock;
+        };
+        const uint32_t buf0 = smem_u32(smem + L.ring0) + team * kChunkBytes;
+        const uint32_t buf1 = smem_u32(smem + L.ring1) + team * kChunkBytes;
+        uint64_t* team_bar = bar + 2 * team;
+        const uint32_t lane_base = stage + (static_cast<uint32_t>(r & ~31) << 16);
+
+        uint32_t consumed[2] = {0u, 0u};
+        auto issue = [&](int q) {
+            if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
+            const int b = q & 1;
+            bulk_load(b ? buf1 : buf0, h.trees + static_cast<size_t>(chunk_at(q)) * kChunkBytes, kChunkBytes,
+                      &team_bar[b]);
+            atomicAdd(&fills[2 * team + b], 1u);
+        };
+        if (issuer && blockIdx.x < groups) {
+            if (n_team > 0) issue(0);
+            if (n_team > 1) issue(1);
+        }
+
+        const uint32_t col = smem_u32(keys) + r * 4;  // this row's key column
+        bool bad = false;                              // the CTA is aborting (uniform after each walkers' barrier)
+        int it = 0;
+        for (long long g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+            const long long row = g * R + r;
+            {
+                // Keys of this group: this row's staged slots c, c + 1, ...
+                // (16 at a time, the team's quarter) from TMEM into the table.
+                const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(full, it & 1, a.wait_ns, abort));
+                if (ok) {
+                    tmem_fence_after_sync();
+                    for (int c = 16 * team; c < staged; c += 16 * kTeams) {
+                        int v[16];
+                        tmem_ld16(lane_base + static_cast<uint32_t>(c), v);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (c + j < staged) keys[(c + j) * R + r] = v[j];
+                        }
+                    }
+                    if (team == 0) keys[a.pad_slot * R + r] = INT_MIN;
+                    tmem_fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty);
+                } else if (lane == 0) {
+                    *abort = 1;
+                }
+            }
+            if (walkers_sync_or(*abort)) {
+                bad = true;
+                break;
+            }
+
+            double acc = 0.0;  // team 0: the row's sum over the rounds done
+            int q = 0;         // position in the team's chunk list
+            for (int k = 0; k < rounds; ++k) {
+                const int block = team + kTeams * k;
+                if (block < blocks) {
+                    const int c0 = block * kChunksPerBlock;
+                    const int cn = min(kChunksPerBlock, chunks - c0);
+                    double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+                    for (int c = 0; c < cn; ++c, ++q) {
+                        const int b = q & 1;
+                        const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u,
+                                                                                     a.wait_ns, abort));
+                        ++consumed[b];
+                        if (ok) {
+                            walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
+                                                     min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
+                        } else if (lane == 0) {
+                            *abort = 1;
+                        }
+                        __syncwarp();
+                        if (lane == 0) {
+                            __threadfence_block();
+                            const unsigned before = atomicAdd(&done[2 * team + b], 1u);
+                            if (before % kWarpsPerTeam == kWarpsPerTeam - 1 && q + 2 < n_team && !*abort) {
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                issue(q + 2);
+                            }
+                        }
+                    }
+                    parts[((k & 1) * kTeams + team) * R + r] = part;
+                }
+                if (walkers_sync_or(*abort)) {
+                    bad = true;
+                    break;
+                }
+                if (team == 0) {
+#pragma unroll
+                    for (int j = 0; j < kTeams; ++j) {
+                        const int blk = kTeams * k + j;
+                        if (blk < blocks) {
+                            const double v = parts[((k & 1) * kTeams + j) * R + r];
+                            acc = blk == 0 ? v : __dadd_rn(acc, v);
+                        }
+                    }
+                }
+            }
+            if (bad) break;
+            if (team == 0 && row < batch) {
+                double v[1] = {acc};
+                if (a.mean) {
+                    const int n = __ldg(a.counts);
+                    v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
+                }
+                apply_link<1>(a, v, 1);
+                out[row] = v[0];
+            }
+            if (issuer && g + gridDim.x < groups) {
+                if (n_team > 0) issue(0);
+                if (n_team > 1) issue(1);
+            }
+            walkers_sync();  // keys and partials are rewritten by the next group
+        }
+        if (bad && issuer) {
+            // Leave no bulk copy in flight into shared memory: wait (bounded)
+            // for the last copy issued to each buffer.
+            if (team == 0) atomicExch(a.status, 1);
+            for (int b = 0; b < 2; ++b) {
+                const unsigned n = fills[2 * team + b];
+                if (n > 0) mbar_wait(&team_bar[b], (n - 1u) & 1u, a.wait_ns);
+            }
+        }
+    }
+    // Every TMEM access of the CTA is done: free the stage.
+    tmem_fence_before_sync();
+    __syncthreads();
+    if (warp == kWalkers / 32) {
+        tmem_fence_after_sync();
+        tmem_dealloc(stage, static_cast<uint32_t>(cols));
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Tree-parallel kernel for small batches (at most kLatencyRows rows), where
 // the row-streaming kernel would give one CTA the whole ensemble. CTA
 // (b, g) takes the 64-tree block b for the (at most) 8 rows of group g, so a
@@ -570,6 +839,30 @@ void* pick_rows(int rows, bool leaf32, bool f64) {
     return nullptr;
 }
 
+template <int D>
+void* pick_staged_leaf(bool leaf32, bool f64) {
+    if (leaf32) {
+        return f64 ? reinterpret_cast<void*>(&heap_staged_kernel<D, true, double>)
+                   : reinterpret_cast<void*>(&heap_staged_kernel<D, true, float>);
+    }
+    return f64 ? reinterpret_cast<void*>(&heap_staged_kernel<D, false, double>)
+               : reinterpret_cast<void*>(&heap_staged_kernel<D, false, float>);
+}
+
+void* pick_staged(int depth, bool leaf32, bool f64) {
+    switch (depth) {
+        case 1: return pick_staged_leaf<1>(leaf32, f64);
+        case 2: return pick_staged_leaf<2>(leaf32, f64);
+        case 3: return pick_staged_leaf<3>(leaf32, f64);
+        case 4: return pick_staged_leaf<4>(leaf32, f64);
+        case 5: return pick_staged_leaf<5>(leaf32, f64);
+        case 6: return pick_staged_leaf<6>(leaf32, f64);
+        case 7: return pick_staged_leaf<7>(leaf32, f64);
+        case 8: return pick_staged_leaf<8>(leaf32, f64);
+    }
+    return nullptr;
+}
+
 void* pick_heap(int depth, int rows, bool leaf32, bool f64) {
     switch (depth) {
         case 1: return pick_rows<1>(rows, leaf32, f64);
@@ -611,14 +904,34 @@ bool heap_plan(int slots, int depth, bool leaf32, int& rows, int& buffers) {
     return false;
 }
 
+namespace {
+
+// Rows per CTA of a complete-tree launch: the plan's, halved while the batch
+// would leave SMs idle.
+int heap_rows(const DevForest& f, long long batch) {
+    int rows = f.heap.rows;
+    while (rows > 32 && (batch + rows - 1) / rows < f.sm_count) rows /= 2;
+    return rows;
+}
+
+}  // namespace
+
+// 128 rows per CTA: the staged kernel, whose producer warps prepare the next
+// group's keys in TMEM while the walkers walk. Its 640 threads take most of
+// an SM's registers, so it runs one CTA per SM and its TMEM allocation never
+// waits for another CTA's.
+bool heap_staged(const DevForest& f, long long batch) {
+    return heap_rows(f, batch) == kStageRows && stage_cols(f.args.pad_slot) > 0;
+}
+
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                  std::string& err) {
     const HeapArgs& h = f.heap;
     const bool f64 = dtype == 2;
-    // Fewer rows per CTA while the batch would leave SMs idle.
-    int rows = h.rows;
-    while (rows > 32 && (batch + rows - 1) / rows < f.sm_count) rows /= 2;
-    void* k = pick_heap(h.depth, rows, h.leaf32, f64);
+    const int rows = heap_rows(f, batch);
+    const int cols = stage_cols(f.args.pad_slot);
+    const bool staged = heap_staged(f, batch);
+    void* k = staged ? pick_staged(h.depth, h.leaf32, f64) : pick_heap(h.depth, rows, h.leaf32, f64);
     if (!k) {
         err = "no complete-tree kernel for this model";
         return false;
@@ -638,13 +951,14 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
         }
     }
     const long long groups = (batch + rows - 1) / rows;
-    const int per_sm = std::max(1, kHeapSmemLimit / (smem + 1024));
+    const int per_sm = staged ? 1 : std::max(1, kHeapSmemLimit / (smem + 1024));
     const int grid = static_cast<int>(std::min<long long>(groups, static_cast<long long>(f.sm_count) * per_sm));
     ForestArgs a = f.args;
     HeapArgs hh = h;
     hh.rows = rows;
-    void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out};
-    const cudaError_t e = cudaLaunchKernel(k, grid, kTeams * rows, args, smem, stream);
+    int stage = cols;
+    void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out, &stage};
+    const cudaError_t e = cudaLaunchKernel(k, grid, staged ? kStagedThreads : kTeams * rows, args, smem, stream);
     if (e != cudaSuccess) {
         err = std::string("complete-tree kernel launch: ") + cudaGetErrorString(e);
         return false;

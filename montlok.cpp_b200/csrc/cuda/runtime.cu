@@ -289,6 +289,8 @@ struct CachedGraph {
     unsigned long long used = 0;
 };
 
+constexpr size_t kCounterBytes = 2 * kLatencyCounters * sizeof(int);  // a workspace's counters: one block per stream
+
 struct Workspace {
     cudaStream_t stream[2] = {nullptr, nullptr};
     // The status word of this thread's host calls (mapped pinned memory): the
@@ -297,7 +299,10 @@ struct Workspace {
     int* status_host = nullptr;
     int* status_dev = nullptr;
     DeviceBuffer dx[2], dout[2], scratch;
-    DeviceBuffer counters;  // the small-batch kernel's counters: zero between launches, nothing else uses them
+    // The small-batch kernel's counters, one block of kLatencyCounters per
+    // stream: zero between launches, nothing else uses them. Always this
+    // size (never reallocated), since cached graphs hold its address.
+    DeviceBuffer counters;
     PinnedBuffer hx[2], hout[2];
     std::vector<CachedGraph> graphs;
     unsigned long long tick = 0;
@@ -368,7 +373,7 @@ int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_
     const size_t in_bytes = batch * static_cast<size_t>(f.args.F) * (dtype == 1 ? 4 : 8);
     const size_t out_bytes = batch * static_cast<size_t>(f.args.K) * sizeof(double);
     const size_t scratch = scratch_bytes(f, static_cast<long long>(batch));
-    if (!w->counters.reserve(kLatencyCounters * sizeof(int), e) || !w->dx[0].reserve(in_bytes, e) ||
+    if (!w->counters.reserve(kCounterBytes, e) || !w->dx[0].reserve(in_bytes, e) ||
         !w->hx[0].reserve(in_bytes, e) ||
         !w->hout[0].reserve(out_bytes, e) || (scratch && !w->scratch.reserve(scratch, e))) {
         put_error(err, errlen, e);
@@ -392,7 +397,8 @@ int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_
         bool good = copy_async(w->dx[0].p, w->hx[0].p, in_bytes, cudaMemcpyHostToDevice, st, e) &&
                     launch_forest(f, dtype, w->dx[0].p, static_cast<long long>(batch),
                                   static_cast<double*>(w->hout[0].p), nullptr, st, e,
-                                  static_cast<int*>(w->scratch.p), static_cast<int*>(w->counters.p)) &&
+                                  scratch ? static_cast<int*>(w->scratch.p) : nullptr,
+                                  static_cast<int*>(w->counters.p)) &&
                     ok(cudaStreamSynchronize(st), "cudaStreamSynchronize", e);
         if (good && *reinterpret_cast<volatile int*>(w->status_host) != 0) {
             e = "a predict kernel gave up waiting for its tree data (bounded wait ran out)";
@@ -417,7 +423,8 @@ int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_
             // buffer (host memory the device addresses directly).
             good = good && launch_forest(f, dtype, kernel_x, static_cast<long long>(batch),
                                          static_cast<double*>(w->hout[0].p), nullptr, st, e,
-                                         static_cast<int*>(w->scratch.p), static_cast<int*>(w->counters.p));
+                                         scratch ? static_cast<int*>(w->scratch.p) : nullptr,
+                                         static_cast<int*>(w->counters.p));
             cudaGraph_t graph = nullptr;
             const cudaError_t end = cudaStreamEndCapture(st, &graph);
             if (good) good = ok(end, "cudaStreamEndCapture", e);
@@ -552,10 +559,14 @@ int run_host(const DevForest& base, int dtype, const void* x, size_t batch, Out*
     const size_t row_dev = narrow ? static_cast<size_t>(f.args.F) * 4 : row_in;
 
     // Chunks are `chunk` rows but the last one, which may take another kernel.
+    // The two streams' kernels may run at the same time, so each stream has
+    // its own half of the scratch (key tables, small-batch sums) and of the
+    // counters.
     const size_t tail = batch % chunk;
-    const size_t scratch = std::max(scratch_bytes(f, static_cast<long long>(chunk)),
-                                    tail ? scratch_bytes(f, static_cast<long long>(tail)) : size_t{0});
-    if ((scratch && !w->scratch.reserve(scratch, e)) || !w->counters.reserve(kLatencyCounters * sizeof(int), e)) {
+    const size_t scratch = (std::max(scratch_bytes(f, static_cast<long long>(chunk)),
+                                     tail ? scratch_bytes(f, static_cast<long long>(tail)) : size_t{0}) +
+                            255) & ~size_t{255};
+    if ((scratch && !w->scratch.reserve(2 * scratch, e)) || !w->counters.reserve(kCounterBytes, e)) {
         put_error(err, errlen, e);
         return kInternal;
     }
@@ -608,9 +619,10 @@ int run_host(const DevForest& base, int dtype, const void* x, size_t batch, Out*
             good = false;
             break;
         }
+        int* own_scratch = scratch ? reinterpret_cast<int*>(static_cast<char*>(w->scratch.p) + s * scratch) : nullptr;
         good = launch_forest(f, kernel_dtype, dsrc, static_cast<long long>(rows), leaves ? nullptr : static_cast<double*>(dst_dev),
-                             leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, static_cast<int*>(w->scratch.p),
-                             static_cast<int*>(w->counters.p));
+                             leaves ? static_cast<int*>(dst_dev) : nullptr, st, e, own_scratch,
+                             static_cast<int*>(w->counters.p) + s * kLatencyCounters);
         if (!good) break;
         if (!dev_out) {
             if (pin_out) {

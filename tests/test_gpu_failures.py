@@ -28,6 +28,8 @@ pytestmark = pytest.mark.gpu
 
 CASES = {
     "complete-tree": (lambda: synth.model_c2(trees=300).to_bytes(), lambda: synth.inputs_c2(batch=5000)),
+    # 128 rows per CTA: the producer warps' TMEM stage beside the walkers
+    "complete-tree-staged": (lambda: synth.model_c2(trees=300).to_bytes(), lambda: synth.inputs_c2(batch=40000)),
     "multi-output": (lambda: synth.model_c4(rounds=12).to_bytes(), lambda: synth.inputs_c4(batch=3000)),
 }
 

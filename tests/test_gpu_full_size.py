@@ -53,6 +53,34 @@ def test_c2_full_size_heap_kernel(gpu, rows):
     check(model, edge_rows(model, synth.inputs_c2(batch=rows), 21), "complete-tree")
 
 
+# Batches of at least 148 x 128 rows keep 128 rows per CTA: the staged kernel,
+# whose producer warps prepare each CTA's next row group in tensor memory.
+# 40,000 rows are 313 groups, two or three per CTA, the last one partial.
+STAGED_ROWS = 40_000
+
+
+def test_c2_full_size_staged_kernel(gpu):
+    model = full_model("c2")
+    check(model, edge_rows(model, synth.inputs_c2(batch=STAGED_ROWS), 23), "complete-tree-staged")
+
+
+@pytest.mark.parametrize("trees", [257, 777])
+@pytest.mark.parametrize("cast, decision", [("f32", "lt"), ("f64", "le")])
+def test_staged_kernel_every_missing_mode(gpu, trees, cast, decision):
+    """Every missing mode (all four key variants of a feature staged),
+    infinite thresholds, float32 and float64 features, partial blocks and
+    rounds, float64 and float32 inputs."""
+    rng = np.random.default_rng([trees, len(cast), len(decision), 1])
+    model = random_model(rng, features=9, trees=trees, max_depth=8, cast=cast, decision=decision,
+                         inf_thresholds=0.05, link="sigmoid", base=0.4)
+    x = near_thresholds(model, rng.normal(size=(STAGED_ROWS + 77, 9)), rng, frac=0.2)
+    x[rng.random(x.shape) < 0.05] = np.nan
+    x[rng.random(x.shape) < 0.02] = 0.0
+    check(model, x, "complete-tree-staged", leaves=False)
+    x32 = x.astype(np.float32)
+    assert same_bits(montlok.load(model).predict(x32).reshape(-1, 1), Oracle(model).predict(x32))
+
+
 def test_c5_full_size_heap_kernel(gpu):
     """1000 trees with preprocessing: 16 blocks, 4 rounds, at a batch above
     the small-batch kernel's."""

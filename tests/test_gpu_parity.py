@@ -252,6 +252,22 @@ def test_many_features_use_global_key_tables(gpu):
     check(model, edge_inputs(rng, 300, 1200, special=0.3))
 
 
+def test_wide_rows_over_several_pipelined_chunks(gpu):
+    """A host call is cut into 64 MB chunks that alternate between two
+    streams; with 3000 float64 features a chunk is 2796 rows, so 5597 rows
+    run three chunks, two of them at once, each with its own global key
+    tables."""
+    rng = np.random.default_rng(31)
+    model = random_model(rng, features=3000, trees=40, max_depth=10)
+    x = edge_inputs(rng, 2 * 2796 + 5, 3000, special=0.3)
+    o, m = Oracle(model), montlok.load(model)
+    want = o.predict(x)
+    assert m.kernel(len(x)) == "generic-global-keys"
+    for _ in range(2):
+        assert same_bits(m.predict(x).reshape(want.shape), want)
+    np.testing.assert_array_equal(m.predict_leaves(x), o.leaves(x))
+
+
 def test_device_buffers_match_host_buffers(gpu):
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(4)
