@@ -99,7 +99,7 @@ __device__ __noinline__ uint32_t walk_exact(const ForestArgs& a, const DeepArgs&
 }
 
 template <bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kWarps * 32, kMinCtas) deep_kernel(const ForestArgs a, const DeepArgs d,
+__global__ void __launch_bounds__(kWarps * 32, kMinCtas) deep_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ DeepArgs d,
                                                             const XT* __restrict__ x, long long batch,
                                                             double* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];

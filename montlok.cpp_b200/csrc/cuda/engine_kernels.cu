@@ -115,7 +115,7 @@ __device__ __forceinline__ void store_release_gpu(unsigned int* p, unsigned int 
 
 template <int D, bool LEAF32>
 __global__ void __launch_bounds__(kEngineThreads, 1)
-    engine_kernel(const ForestArgs a, const HeapArgs h, Mailbox* box, const double* x, double* out, double* bpart,
+    engine_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ HeapArgs h, Mailbox* box, const double* x, double* out, double* bpart,
                   double* xd, Relay* relay, unsigned int first) {
     Answer* answers = reinterpret_cast<Answer*>(out);
     constexpr int kRec = heap_record_size(D, LEAF32);

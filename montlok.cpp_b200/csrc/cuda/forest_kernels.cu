@@ -90,7 +90,7 @@ __device__ __forceinline__ void walk_block(const ForestArgs& a, const int* col, 
 }
 
 template <bool TIES, bool LEAVES, int KC, bool GLOBAL_KEYS, typename XT>
-__global__ void __launch_bounds__(64) forest_kernel(const ForestArgs a, const XT* __restrict__ x, long long batch,
+__global__ void __launch_bounds__(64) forest_kernel(const __grid_constant__ ForestArgs a, const XT* __restrict__ x, long long batch,
                                                      double* __restrict__ out, int* __restrict__ leaves, int k0,
                                                      int kc, int link_here, int* __restrict__ scratch) {
     extern __shared__ __align__(16) unsigned char smem[];

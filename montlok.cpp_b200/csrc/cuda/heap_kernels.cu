@@ -170,7 +170,7 @@ __device__ __forceinline__ void walk_chunk(const ForestArgs& a, const HeapArgs& 
 }
 
 template <int D, int R, bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a, const HeapArgs h,
+__global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ HeapArgs h,
                                                           const XT* __restrict__ x, long long batch,
                                                           double* __restrict__ out) {
     constexpr int kChunkBytes = kTrees * record_bytes(D, LEAF32);
@@ -221,9 +221,9 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
     __syncthreads();
 
     // Buffer b's k-th fill completes its barrier's phase k: every thread of
-    // the team counts the fills it has consumed; `fills` counts those issued
-    // (to wait out copies in flight before an early exit).
-    uint32_t consumed[2] = {0u, 0u};
+    // the team keeps the parity of the next fill it waits for; `fills`
+    // counts those issued (to wait out copies in flight before an early exit).
+    uint32_t phase = 0u;  // bit b: parity of the next fill of buffer b (a register, not an indexed array)
     auto issue = [&](int q) {
         if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
         const int b = q & 1;
@@ -269,9 +269,9 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const ForestArgs a,
                     // CTA is aborting no wait is trusted: a warp whose own wait
                     // ran out has lost count of the barrier's phases, and a
                     // wait on the other parity would return at once.
-                    const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u,
+                    const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], (phase >> b) & 1u,
                                                                                  a.wait_ns, abort));
-                    ++consumed[b];
+                    phase ^= 1u << b;
                     if (ok) {
                         walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
                                                  min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
@@ -386,7 +386,7 @@ __host__ __device__ inline int stage_cols(int pad_slot) {
 }
 
 template <int D, bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const ForestArgs a, const HeapArgs h,
+__global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ HeapArgs h,
                                                                         const XT* __restrict__ x, long long batch,
                                                                         double* __restrict__ out, int cols) {
     constexpr int R = kStageRows;
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const Fo
         uint64_t* team_bar = bar + 2 * team;
         const uint32_t lane_base = stage + (static_cast<uint32_t>(r & ~31) << 16);
 
-        uint32_t consumed[2] = {0u, 0u};
+        uint32_t phase = 0u;  // bit b: parity of the next fill of buffer b (a register, not an indexed array)
         auto issue = [&](int q) {
             if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
             const int b = q & 1;
@@ -535,9 +535,9 @@ __global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const Fo
                     double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
                     for (int c = 0; c < cn; ++c, ++q) {
                         const int b = q & 1;
-                        const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u,
+                        const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], (phase >> b) & 1u,
                                                                                      a.wait_ns, abort));
-                        ++consumed[b];
+                        phase ^= 1u << b;
                         if (ok) {
                             walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
                                                      min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
@@ -665,7 +665,7 @@ __device__ __forceinline__ uint32_t walk_global(const ForestArgs& a, const HeapA
 }
 
 template <int D, bool LEAF32, typename XT>
-__global__ void __launch_bounds__(kLatencyThreads) latency_kernel(const ForestArgs a, const HeapArgs h,
+__global__ void __launch_bounds__(kLatencyThreads) latency_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ HeapArgs h,
                                                                   const XT* __restrict__ x, long long batch,
                                                                   double* __restrict__ out, double* bpart, int* count) {
     constexpr int kRec = record_bytes(D, LEAF32);

@@ -162,7 +162,7 @@ __device__ __noinline__ uint32_t walk_exact(const ForestArgs& a, const SparseArg
 }
 
 template <int R, int TEAMS, bool LEAF32, typename XT>
-__global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a, const SparseArgs s,
+__global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ SparseArgs s,
                                                                    const XT* __restrict__ x, long long batch,
                                                                    double* __restrict__ out) {
     constexpr int kWarpsPerTeam = R / 32;
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
     }
     __syncthreads();
 
-    uint32_t consumed[2] = {0u, 0u};
+    uint32_t phase = 0u;  // bit b: parity of the next fill of buffer b (a register, not an indexed array)
     auto issue = [&](int q) {
         if (a.skip_copies) return;  // fault injection: the wait for this chunk runs out
         const int b = q & 1;
@@ -247,9 +247,9 @@ __global__ void __launch_bounds__(TEAMS * R, 1) sparse_kernel(const ForestArgs a
             // Once the CTA is aborting no wait is trusted: a warp whose own
             // wait ran out has lost count of the barrier's phases, and a wait
             // on the other parity would return at once.
-            const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], consumed[b] & 1u, a.wait_ns,
+            const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], (phase >> b) & 1u, a.wait_ns,
                                                                          abort));
-            ++consumed[b];
+            phase ^= 1u << b;
             if (ok) {
                 const uint32_t buf = b ? buf1 : buf0;
                 int4 hdr[kTrees];
