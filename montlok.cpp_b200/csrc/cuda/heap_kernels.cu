@@ -72,11 +72,13 @@ struct Layout {
     int keys, parts, ring0, ring1, total;
 };
 
-__host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, int rows) {
+// `partials` rows of partial sums: 2 * kTeams (two rounds of four blocks)
+// for heap_kernel, one per 64-tree block for the staged kernel.
+__host__ __device__ inline Layout layout_of(int slots, int depth, bool leaf32, int rows, int partials = 2 * kTeams) {
     Layout l{};
     l.keys = 256;
     l.parts = l.keys + align128(slots * rows * 4);
-    l.ring0 = l.parts + align128(2 * kTeams * rows * 8);
+    l.ring0 = l.parts + align128(partials * rows * 8);
     const int chunk = kTrees * record_bytes(depth, leaf32);
     l.ring1 = l.ring0 + align128(kTeams * chunk);
     l.total = l.ring1 + align128(kTeams * chunk);
@@ -351,8 +353,10 @@ __global__ void __launch_bounds__(kTeams * R, 1) heap_kernel(const __grid_consta
 // hand the stage over: `full` (one arrival per producer warp: the group's
 // keys are in TMEM) and `empty` (one per walker warp: copied out, the stage
 // may be overwritten). Each is waited on with the time bound and abort flag
-// of the chunk waits; the walkers' round barriers are a named barrier of the
-// 512 walkers, the producers never take part in them. The CTA allocates the
+// of the chunk waits. Every 64-tree block's partial sums have their own row
+// of shared memory, so the walkers meet once per group (a named barrier of
+// the 512 walkers; the producers never take part), after which team 0 adds
+// the blocks in order. The CTA allocates the
 // stage's TMEM columns once and frees them on every way out, after a last
 // barrier of all 640 threads. Only for 128 rows per CTA and models whose pad
 // slot is at most 512 (the stage fits 512 columns); one CTA per SM (its
@@ -377,6 +381,11 @@ __device__ __forceinline__ bool walkers_sync_or(int v) {
 }
 __device__ __forceinline__ void walkers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWalkers) : "memory"); }
 
+// Rows of partial sums the staged kernel keeps: one per 64-tree block.
+__host__ __device__ inline int stage_partials(int trees) {
+    return max(2 * kTeams, (trees + kTreeBlock - 1) / kTreeBlock);
+}
+
 // TMEM columns a model's stage takes: the smallest power of two, at least
 // 32, holding slots 0 .. pad_slot - 1; 0 when it needs more than 512.
 __host__ __device__ inline int stage_cols(int pad_slot) {
@@ -393,7 +402,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const __
     constexpr int kChunkBytes = kTrees * record_bytes(D, LEAF32);
     constexpr int kWarpsPerTeam = R / 32;
     extern __shared__ __align__(128) unsigned char smem[];
-    const Layout L = layout_of(a.slots, D, LEAF32, R);
+    const Layout L = layout_of(a.slots, D, LEAF32, R, stage_partials(a.T));
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                // [team][buffer]
     unsigned* done = reinterpret_cast<unsigned*>(smem + 64);         // [team][buffer]: warps done, cumulative
     unsigned* fills = reinterpret_cast<unsigned*>(smem + 96);        // [team][buffer]: copies issued
@@ -469,7 +478,6 @@ __global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const __
         const bool issuer = r == 0;  // issues the team's first two copies of a row group
         const int chunks = (a.T + kTrees - 1) / kTrees;
         const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;
-        const int rounds = (blocks + kTeams - 1) / kTeams;
         int n_team = 0;
         for (int b = team; b < blocks; b += kTeams) n_team += min(kChunksPerBlock, chunks - b * kChunksPerBlock);
         auto chunk_at = [&](int q) {
@@ -525,54 +533,43 @@ __global__ void __launch_bounds__(kStagedThreads, 1) heap_staged_kernel(const __
                 break;
             }
 
-            double acc = 0.0;  // team 0: the row's sum over the rounds done
-            int q = 0;         // position in the team's chunk list
-            for (int k = 0; k < rounds; ++k) {
-                const int block = team + kTeams * k;
-                if (block < blocks) {
-                    const int c0 = block * kChunksPerBlock;
-                    const int cn = min(kChunksPerBlock, chunks - c0);
-                    double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
-                    for (int c = 0; c < cn; ++c, ++q) {
-                        const int b = q & 1;
-                        const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], (phase >> b) & 1u,
-                                                                                     a.wait_ns, abort));
-                        phase ^= 1u << b;
-                        if (ok) {
-                            walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
-                                                     min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
-                        } else if (lane == 0) {
-                            *abort = 1;
-                        }
-                        __syncwarp();
-                        if (lane == 0) {
-                            __threadfence_block();
-                            const unsigned before = atomicAdd(&done[2 * team + b], 1u);
-                            if (before % kWarpsPerTeam == kWarpsPerTeam - 1 && q + 2 < n_team && !*abort) {
-                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                                issue(q + 2);
-                            }
-                        }
+            // Every block's partial has its own row of `parts`: the teams
+            // meet once per group, after all their blocks.
+            int q = 0;  // position in the team's chunk list
+            for (int block = team; block < blocks; block += kTeams) {
+                const int c0 = block * kChunksPerBlock;
+                const int cn = min(kChunksPerBlock, chunks - c0);
+                double part = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+                for (int c = 0; c < cn; ++c, ++q) {
+                    const int b = q & 1;
+                    const bool ok = __all_sync(0xffffffffu, !*abort && mbar_wait(&team_bar[b], (phase >> b) & 1u,
+                                                                                 a.wait_ns, abort));
+                    phase ^= 1u << b;
+                    if (ok) {
+                        walk_chunk<D, R, LEAF32>(a, h, b ? buf1 : buf0, col, mask, c0 + c,
+                                                 min(kTrees, a.T - (c0 + c) * kTrees), x, row, batch, part);
+                    } else if (lane == 0) {
+                        *abort = 1;
                     }
-                    parts[((k & 1) * kTeams + team) * R + r] = part;
-                }
-                if (walkers_sync_or(*abort)) {
-                    bad = true;
-                    break;
-                }
-                if (team == 0) {
-#pragma unroll
-                    for (int j = 0; j < kTeams; ++j) {
-                        const int blk = kTeams * k + j;
-                        if (blk < blocks) {
-                            const double v = parts[((k & 1) * kTeams + j) * R + r];
-                            acc = blk == 0 ? v : __dadd_rn(acc, v);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        const unsigned before = atomicAdd(&done[2 * team + b], 1u);
+                        if (before % kWarpsPerTeam == kWarpsPerTeam - 1 && q + 2 < n_team && !*abort) {
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            issue(q + 2);
                         }
                     }
                 }
+                parts[block * R + r] = part;
             }
-            if (bad) break;
+            if (walkers_sync_or(*abort)) {
+                bad = true;
+                break;
+            }
             if (team == 0 && row < batch) {
+                double acc = parts[r];  // blocks in order: the reference's association
+                for (int blk = 1; blk < blocks; ++blk) acc = __dadd_rn(acc, parts[blk * R + r]);
                 double v[1] = {acc};
                 if (a.mean) {
                     const int n = __ldg(a.counts);
@@ -921,7 +918,9 @@ int heap_rows(const DevForest& f, long long batch) {
 // an SM's registers, so it runs one CTA per SM and its TMEM allocation never
 // waits for another CTA's.
 bool heap_staged(const DevForest& f, long long batch) {
-    return heap_rows(f, batch) == kStageRows && stage_cols(f.args.pad_slot) > 0;
+    return heap_rows(f, batch) == kStageRows && stage_cols(f.args.pad_slot) > 0 &&
+           layout_of(f.args.slots, f.heap.depth, f.heap.leaf32, kStageRows, stage_partials(f.args.T)).total <=
+               kHeapSmemLimit;
 }
 
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
@@ -936,7 +935,8 @@ bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, 
         err = "no complete-tree kernel for this model";
         return false;
     }
-    const int smem = layout_of(f.args.slots, h.depth, h.leaf32, rows).total;
+    const int smem =
+        layout_of(f.args.slots, h.depth, h.leaf32, rows, staged ? stage_partials(f.args.T) : 2 * kTeams).total;
     {
         static std::mutex mu;
         static std::vector<std::pair<void*, int>> set;
