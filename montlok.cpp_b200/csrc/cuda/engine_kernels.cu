@@ -8,14 +8,15 @@
 // Each CTA of the engine owns one 64-tree block of a complete-tree forest and
 // keeps its tree records in shared memory for its whole life, so a walk is
 // eight shared loads. The calling thread writes the request's rows into a
-// mailbox in pinned host memory and bumps its sequence number. Thread 0 of
-// CTA 0 polls that number (system-scope acquire loads; the only poller of the
-// bus), CTA 0 reads the rows over the bus in 16-byte loads and relays them
-// through device memory, publishing the number in a device-memory word the
-// other CTAs poll. Every CTA then builds the rows' keys, walks its 64 trees
+// mailbox in pinned host memory and posts its number and row count in one
+// 64-bit word. Thread 0 of CTA 0 polls that word (system-scope acquire loads;
+// the only poller of the bus), CTA 0 reads the rows over the bus in 16-byte
+// loads and relays them through device memory, publishing the word in device
+// memory (a release store the other CTAs poll with acquire loads). Every CTA then builds the rows' keys, walks its 64 trees
 // for each row (one thread per tree and row pair) and adds the leaves in tree
 // order into its block's partial sum. The last CTA to finish (a device-scope
-// counter, no waiting) adds the block sums in block order, applies the link
+// acquire-release counter, no waiting) loads the block sums sixteen at a time
+// and adds them in block order, applies the link
 // and writes each row's answer into the mailbox as one 16-byte record with
 // the request's number; the caller spins on those numbers.
 //
@@ -50,12 +51,17 @@ constexpr long long kEngineCheckNs = 20000000ll;            // when the host fir
 static_assert(kEngineRows == 2 * kEnginePairs, "each thread walks two rows");
 
 // The mailbox, in pinned host memory the engine reads and writes over the bus.
+// A request is posted as one 64-bit store of its number (low half) and rows
+// (high half), so one bus read brings both.
 struct Mailbox {
-    unsigned int seq;   // host: number of the latest request
-    unsigned int done;  // engine: unused (answers carry their own number)
-    unsigned int stop;  // host: exit now
-    int rows;           // host: rows of the latest request
+    unsigned long long post;  // host: rows << 32 | number of the latest request
+    unsigned int stop;        // host: exit now
+    unsigned int unused;
 };
+
+__host__ __device__ inline unsigned long long post_word(unsigned int seq, int rows) {
+    return static_cast<unsigned long long>(static_cast<unsigned int>(rows)) << 32 | seq;
+}
 
 // One row's answer, written with a single 16-byte store: the caller reads
 // `value` once `seq` shows its request's number, so the engine needs no
@@ -70,6 +76,11 @@ __device__ __forceinline__ unsigned int load_acquire_sys(const unsigned int* p) 
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ unsigned long long load_acquire_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // A request value read past any cache: the host rewrites these each call.
 __device__ __forceinline__ double load_fresh(const double* p) {
@@ -78,10 +89,15 @@ __device__ __forceinline__ double load_fresh(const double* p) {
     return v;
 }
 
+// Shared memory: control words | the block's tree records | keys [slot][row]
+// | rows [row][F] | leaf values [tree][row] | per feature its slots (int4),
+// preprocessing mean and scale (copied once, so a request reads no constant
+// from global memory).
 __host__ __device__ inline int engine_smem(int slots, int F, int record) {
     return 128 + kTreeBlock * record + align128(slots * kEngineRows * 4) + align128(kEngineRows * F * 8) +
-           kTreeBlock * kEngineRows * 8;
+           kTreeBlock * kEngineRows * 8 + align128(F * 32);
 }
+
 
 // The split decided on the double for a float64 model whose keys tied (the
 // rows sit in shared memory: `xs` [row][F]).
@@ -97,20 +113,28 @@ __device__ __forceinline__ bool exact_split(const ForestArgs& a, const double* x
 // Device-memory side of a request: the rows CTA 0 copied from the mailbox,
 // and the words it publishes them with.
 struct Relay {
-    unsigned int go;    // number of the request whose rows are in `x`
-    int rows;           // its rows
-    int count;          // CTAs done with the current request
-    int quit;           // 1: every CTA leaves
+    unsigned long long go;  // rows << 32 | number of the request whose rows are in `x`
+    int count;              // CTAs done with the current request
+    int quit;               // 1: every CTA leaves
 };
 
-__device__ __forceinline__ unsigned int load_acquire_gpu(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long load_acquire_gpu64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void store_release_gpu(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void store_release_gpu64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Counts this CTA done (release: its block sums, stored before the CTA
+// barrier, are published with it; acquire: the last CTA sees every other
+// CTA's); returns the count before.
+__device__ __forceinline__ int count_done(int* p) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+    return old;
 }
 
 template <int D, bool LEAF32>
@@ -128,6 +152,8 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
                                            align128(a.slots * kEngineRows * 4));  // [row][F]
     double* leafv = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(xs) +
                                               align128(kEngineRows * a.F * 8));   // [tree][row]
+    int4* slot_of = reinterpret_cast<int4*>(leafv + kTreeBlock * kEngineRows);  // [F]
+    double* pre = reinterpret_cast<double*>(slot_of + a.F);                     // [F] mean, scale
 
     const int tid = threadIdx.x;
     const int blocks = gridDim.x, block = blockIdx.x;
@@ -141,6 +167,11 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         const int4* src = reinterpret_cast<const int4*>(h.trees + static_cast<size_t>(t0) * kRec);
         int4* dst = reinterpret_cast<int4*>(trees);
         for (int i = tid; i < nt * kRec / 16; i += kEngineThreads) dst[i] = __ldg(src + i);
+        for (int f = tid; f < a.F; f += kEngineThreads) {
+            slot_of[f] = __ldg(a.slot_of + f);
+            pre[2 * f] = a.standardize ? __ldg(a.pre_mean + f) : 0.0;
+            pre[2 * f + 1] = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
+        }
     }
     __syncthreads();
 
@@ -151,11 +182,16 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             // the bus), the others on CTA 0's relay in device memory; every
             // wait is bounded.
             unsigned int cmd = 0, seq = mine;
+            unsigned long long word = 0;
             const unsigned long long since = global_ns();
             for (long long polls = 0;; ++polls) {
-                seq = block == 0 ? load_acquire_sys(&box->seq) : load_acquire_gpu(&relay->go);
+                word = block == 0 ? load_acquire_sys64(&box->post) : load_acquire_gpu64(&relay->go);
+                seq = static_cast<unsigned int>(word);
                 if (seq != mine) break;
-                if (*quit || polls >= kEnginePolls || (block == 0 && load_acquire_sys(&box->stop))) {
+                // `stop` (a second bus read) is looked at every 256th poll
+                // only, so a poll is one bus round trip.
+                if (*quit || polls >= kEnginePolls ||
+                    (block == 0 && (polls & 255) == 255 && load_acquire_sys(&box->stop))) {
                     cmd = 1;
                     break;
                 }
@@ -171,9 +207,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             if (cmd && block == 0) atomicExch(&relay->quit, 1);
             ctl[0] = seq;
             ctl[1] = cmd;
-            ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, block == 0
-                                                                         ? *reinterpret_cast<volatile int*>(&box->rows)
-                                                                         : *reinterpret_cast<volatile int*>(&relay->rows))));
+            ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, static_cast<int>(word >> 32))));
         }
         __syncthreads();
         if (ctl[1]) return;
@@ -195,20 +229,15 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
                 }
             }
             __syncthreads();
-            if (tid == 0) {
-                relay->rows = rows;
-                __threadfence();
-                store_release_gpu(&relay->go, seq);
-            }
+            // Release: the rows stored into `xd` before the barrier go with it.
+            if (tid == 0) store_release_gpu64(&relay->go, post_word(seq, rows));
         } else {
             for (int i = tid; i < values; i += kEngineThreads) xs[i] = __ldcg(xd + i);
             __syncthreads();
         }
         for (int i = tid; i < values; i += kEngineThreads) {
             const int f = i % a.F;
-            const double mean = a.standardize ? __ldg(a.pre_mean + f) : 0.0;
-            const double scale = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
-            put_keys<kEngineRows>(a, keys + i / a.F, __ldg(a.slot_of + f), finish(a, xs[i], mean, scale),
+            put_keys<kEngineRows>(a, keys + i / a.F, slot_of[f], finish(a, xs[i], pre[2 * f], pre[2 * f + 1]),
                                   static_cast<int>(mask));
         }
         if (tid < kEngineRows) keys[a.pad_slot * kEngineRows + tid] = INT_MIN;
@@ -252,19 +281,31 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
             for (int j = 0; j < nt; ++j) acc = __dadd_rn(acc, leafv[j * kEngineRows + tid]);
             __stcg(bpart + static_cast<size_t>(block) * kEngineRows + tid, acc);
-            __threadfence();
         }
         __syncthreads();
         if (tid == 0) {
-            const bool last = atomicAdd(&relay->count, 1) == blocks - 1;
+            const bool last = count_done(&relay->count) == blocks - 1;
             if (last) relay->count = 0;  // every CTA has counted this request
             ctl[1] = last;
         }
         __syncthreads();
         if (ctl[1]) {
             if (tid < rows) {
-                double v[1] = {__ldcg(bpart + tid)};
-                for (int b = 1; b < blocks; ++b) v[0] = __dadd_rn(v[0], __ldcg(bpart + static_cast<size_t>(b) * kEngineRows + tid));
+                // The block sums, 16 loads in flight at a time, added in
+                // block order.
+                constexpr int kBatch = 16;
+                double v[1] = {0.0};
+                for (int b0 = 0; b0 < blocks; b0 += kBatch) {
+                    double t[kBatch];
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        t[j] = b0 + j < blocks ? __ldcg(bpart + static_cast<size_t>(b0 + j) * kEngineRows + tid) : 0.0;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        if (b0 + j < blocks) v[0] = b0 + j == 0 ? t[j] : __dadd_rn(v[0], t[j]);
+                    }
+                }
                 if (a.mean) {
                     const int n = __ldg(a.counts);
                     v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
@@ -363,7 +404,7 @@ static bool engine_launch(const DevForest& f, LatencyEngine& e, unsigned int fir
     double* xd = bpart + static_cast<size_t>(e.blocks) * kEngineRows;
     Relay* relay = reinterpret_cast<Relay*>(xd + static_cast<size_t>(kEngineRows) * e.F);
     // The relay starts at the request the engine treats as answered.
-    const Relay start{first, 0, 0, 0};
+    const Relay start{first, 0, 0};
     if (!checked(cudaMemcpyAsync(relay, &start, sizeof start, cudaMemcpyHostToDevice, e.stream), "cudaMemcpyAsync",
                  err) ||
         !checked(cudaStreamSynchronize(e.stream), "cudaStreamSynchronize", err)) {
@@ -432,10 +473,9 @@ int engine_predict(const DevForest& f, LatencyEngine*& slot, int dtype, const vo
         std::memcpy(xh, x, values * sizeof(double));
     }
     volatile Mailbox* box = e.box();
-    box->rows = static_cast<int>(batch);
     const unsigned int seq = ++e.seq;
     std::atomic_thread_fence(std::memory_order_seq_cst);
-    box->seq = seq;
+    box->post = post_word(seq, static_cast<int>(batch));  // one aligned 64-bit store
     const long long posted = now_ns();
     long long checked_at = posted + kEngineCheckNs;
     volatile Answer* answers = e.out_host();
