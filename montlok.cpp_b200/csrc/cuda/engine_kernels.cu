@@ -89,13 +89,21 @@ __device__ __forceinline__ double load_fresh(const double* p) {
     return v;
 }
 
-// Shared memory: control words | the block's tree records | keys [slot][row]
-// | rows [row][F] | leaf values [tree][row] | per feature its slots (int4),
-// preprocessing mean and scale (copied once, so a request reads no constant
-// from global memory).
+constexpr int kClusterBlocks = 16;  // engines of at most this many blocks run as one thread-block cluster
+// The cluster form pushes a request's rows into every CTA's shared memory when
+// the copies total at most this many values (c5: requests of 1 or 2 rows);
+// larger requests go through device memory once (CTA 0's port would carry
+// every copy).
+constexpr int kPushValues = 6144;
+
+// Shared memory: control words and the cluster form's two mbarriers | the
+// block's tree records | keys [slot][row] | rows [row][F] | leaf values
+// [tree][row] | per feature its slots (int4), preprocessing mean and scale
+// (copied once, so a request reads no constant from global memory) | the
+// cluster form's block sums [block][row] (used in CTA 0).
 __host__ __device__ inline int engine_smem(int slots, int F, int record) {
     return 128 + kTreeBlock * record + align128(slots * kEngineRows * 4) + align128(kEngineRows * F * 8) +
-           kTreeBlock * kEngineRows * 8 + align128(F * 32);
+           kTreeBlock * kEngineRows * 8 + align128(F * 32) + kClusterBlocks * kEngineRows * 8;
 }
 
 
@@ -137,7 +145,63 @@ __device__ __forceinline__ int count_done(int* p) {
     return old;
 }
 
-template <int D, bool LEAF32>
+// Distributed shared memory of a thread-block cluster (the engine's cluster
+// form): the address of a shared variable in CTA `rank`, stores into it, and
+// remote mbarrier arrivals.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f64(uint32_t addr, double v) {
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2f64(uint32_t addr, double v0, double v1) {
+    asm volatile("st.shared::cluster.v2.f64 [%0], {%1, %2};" ::"r"(addr), "d"(v0), "d"(v1) : "memory");
+}
+// Release at cluster scope: the CTA's stores before its barrier reach the
+// waiter with the arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Waits for phase `parity` of a local mbarrier that CTAs of the cluster
+// arrive on; false after `limit_ns`.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned long long limit_ns) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (long long polls = 0; polls < kEnginePolls; ++polls) {
+        if (mbar_try_cluster(bar, parity)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+    return false;
+}
+// Every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// CLUSTER: the engine's CTAs form one thread-block cluster (at most
+// kClusterBlocks). CTA 0 pushes a request's rows and control words into every
+// CTA's shared memory and wakes it with a remote arrival on its `rows_bar`;
+// each CTA pushes its block sums into CTA 0's `bsum` and arrives on CTA 0's
+// `sum_bar`, on which CTA 0 waits before adding them in block order. No
+// device-memory relay, counter or reload of the sums. Without CLUSTER the
+// CTAs meet through device memory (`relay`, `bpart`). An engine CTA leaves
+// only through a cluster barrier, so no CTA leaves while another may still
+// write into its shared memory.
+template <int D, bool LEAF32, bool CLUSTER>
 __global__ void __launch_bounds__(kEngineThreads, 1)
     engine_kernel(const __grid_constant__ ForestArgs a, const __grid_constant__ HeapArgs h, Mailbox* box, const double* x, double* out, double* bpart,
                   double* xd, Relay* relay, unsigned int first) {
@@ -145,7 +209,9 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
     constexpr int kRec = heap_record_size(D, LEAF32);
     constexpr int kSplits = (1 << D) - 1;
     extern __shared__ __align__(128) unsigned char smem[];
-    volatile unsigned int* ctl = reinterpret_cast<volatile unsigned int*>(smem);  // request, exit/last, rows
+    volatile unsigned int* ctl = reinterpret_cast<volatile unsigned int*>(smem);  // request, exit/last, rows, ok
+    uint64_t* rows_bar = reinterpret_cast<uint64_t*>(smem + 64);                 // cluster: a request's rows are in
+    uint64_t* sum_bar = reinterpret_cast<uint64_t*>(smem + 72);                  // cluster, CTA 0: every block summed
     unsigned char* trees = smem + 128;
     int* keys = reinterpret_cast<int*>(trees + kTreeBlock * kRec);  // [slot][kEngineRows]
     double* xs = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(keys) +
@@ -154,6 +220,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
                                               align128(kEngineRows * a.F * 8));   // [tree][row]
     int4* slot_of = reinterpret_cast<int4*>(leafv + kTreeBlock * kEngineRows);  // [F]
     double* pre = reinterpret_cast<double*>(slot_of + a.F);                     // [F] mean, scale
+    double* bsum = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(slot_of) + align128(a.F * 32));  // [block][row]
 
     const int tid = threadIdx.x;
     const int blocks = gridDim.x, block = blockIdx.x;
@@ -173,68 +240,145 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             pre[2 * f + 1] = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
         }
     }
-    __syncthreads();
-
-    unsigned int mine = first;
-    for (;;) {
+    if constexpr (CLUSTER) {
         if (tid == 0) {
-            // CTA 0 waits on the mailbox in host memory (the only poller of
-            // the bus), the others on CTA 0's relay in device memory; every
-            // wait is bounded.
-            unsigned int cmd = 0, seq = mine;
-            unsigned long long word = 0;
-            const unsigned long long since = global_ns();
-            for (long long polls = 0;; ++polls) {
-                word = block == 0 ? load_acquire_sys64(&box->post) : load_acquire_gpu64(&relay->go);
-                seq = static_cast<unsigned int>(word);
-                if (seq != mine) break;
-                // `stop` (a second bus read) is looked at every 256th poll
-                // only, so a poll is one bus round trip.
-                if (*quit || polls >= kEnginePolls ||
-                    (block == 0 && (polls & 255) == 255 && load_acquire_sys(&box->stop))) {
-                    cmd = 1;
-                    break;
-                }
-                // CTA 0 decides when the engine has idled long enough and
-                // tells the others; they also leave on their own after
-                // twice that.
-                if (global_ns() - since > (block == 0 ? 1u : 2u) * kEngineIdleNs) {
-                    cmd = 1;
-                    break;
-                }
-                __nanosleep(block == 0 ? 32 : 16);
-            }
-            if (cmd && block == 0) atomicExch(&relay->quit, 1);
-            ctl[0] = seq;
-            ctl[1] = cmd;
-            ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, static_cast<int>(word >> 32))));
+            mbar_init(rows_bar, 1);
+            mbar_init(sum_bar, static_cast<uint32_t>(blocks));
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         __syncthreads();
-        if (ctl[1]) return;
+        cluster_sync();  // every CTA's barriers exist before any remote arrival
+    } else {
+        __syncthreads();
+    }
+
+    unsigned int mine = first;
+    uint32_t n = 0;  // requests this engine has served (the phase of its barriers)
+    for (;;) {
+        // CTA 0 waits on the mailbox in host memory (the only poller of the
+        // bus); every wait is bounded.
+        if (block == 0) {
+            if (tid == 0) {
+                unsigned int cmd = 0, seq = mine;
+                unsigned long long word = 0;
+                const unsigned long long since = global_ns();
+                for (long long polls = 0;; ++polls) {
+                    word = load_acquire_sys64(&box->post);
+                    seq = static_cast<unsigned int>(word);
+                    if (seq != mine) break;
+                    // `stop` (a second bus read) is looked at every 256th poll
+                    // only, so a poll is one bus round trip.
+                    if ((!CLUSTER && *quit) || polls >= kEnginePolls ||
+                        ((polls & 255) == 255 && load_acquire_sys(&box->stop))) {
+                        cmd = 1;
+                        break;
+                    }
+                    // CTA 0 decides when the engine has idled long enough.
+                    if (global_ns() - since > kEngineIdleNs) {
+                        cmd = 1;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+                if (!CLUSTER && cmd) atomicExch(&relay->quit, 1);
+                ctl[0] = seq;
+                ctl[1] = cmd;
+                ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, static_cast<int>(word >> 32))));
+            }
+            __syncthreads();
+        } else if constexpr (CLUSTER) {
+            // CTA 0 pushes the request (or the order to leave) and arrives;
+            // the bound is a safety net far beyond CTA 0's idle limit.
+            if (tid == 0 && !mbar_wait_cluster(rows_bar, n & 1u, 4 * kEngineIdleNs)) ctl[1] = 1;
+            __syncthreads();
+        } else {
+            if (tid == 0) {
+                unsigned int cmd = 0, seq = mine;
+                unsigned long long word = 0;
+                const unsigned long long since = global_ns();
+                for (long long polls = 0;; ++polls) {
+                    word = load_acquire_gpu64(&relay->go);
+                    seq = static_cast<unsigned int>(word);
+                    if (seq != mine) break;
+                    if (*quit || polls >= kEnginePolls || global_ns() - since > 2 * kEngineIdleNs) {
+                        cmd = 1;
+                        break;
+                    }
+                    __nanosleep(16);
+                }
+                ctl[0] = seq;
+                ctl[1] = cmd;
+                ctl[2] = static_cast<unsigned int>(min(kEngineRows, max(1, static_cast<int>(word >> 32))));
+            }
+            __syncthreads();
+        }
+        const unsigned int cmd = ctl[1];
         const unsigned int seq = ctl[0];
         const int rows = static_cast<int>(ctl[2]);
         const int values = rows * a.F;
+        const bool push = CLUSTER && values * (blocks - 1) <= kPushValues;
         if (block == 0) {
-            // Rows from host memory in 16-byte reads, relayed through device
-            // memory to the other CTAs.
-            const int pairs = (values + 1) / 2;
-            for (int i = tid; i < pairs; i += kEngineThreads) {
-                double2 v;
-                asm volatile("ld.global.cv.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(x + 2 * i) : "memory");
-                xs[2 * i] = v.x;
-                xd[2 * i] = v.x;
-                if (2 * i + 1 < values) {
-                    xs[2 * i + 1] = v.y;
-                    xd[2 * i + 1] = v.y;
+            if (!cmd) {
+                // Rows from host memory in 16-byte reads, into this CTA's
+                // table and (cluster) every other CTA's, or (no cluster)
+                // relayed through device memory.
+                // Four reads in flight per thread before any store (each read
+                // is a bus round trip).
+                constexpr int kInFlight = 4;
+                const int pairs = (values + 1) / 2;
+                for (int i0 = tid; i0 < pairs; i0 += kInFlight * kEngineThreads) {
+                    double2 v[kInFlight];
+#pragma unroll
+                    for (int u = 0; u < kInFlight; ++u) {
+                        const int i = i0 + u * kEngineThreads;
+                        if (i < pairs) {
+                            asm volatile("ld.global.cv.v2.f64 {%0, %1}, [%2];"
+                                         : "=d"(v[u].x), "=d"(v[u].y)
+                                         : "l"(x + 2 * i)
+                                         : "memory");
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < kInFlight; ++u) {
+                        const int i = i0 + u * kEngineThreads;
+                        if (i >= pairs) break;
+                        xs[2 * i] = v[u].x;
+                        if (2 * i + 1 < values) xs[2 * i + 1] = v[u].y;
+                        if (push) {
+                            // pairs are 16-byte aligned ([row][F] doubles); the
+                            // odd value past the end lands in the table's slack
+                            const uint32_t at = smem_u32(xs + 2 * i);
+                            for (int j = 1; j < blocks; ++j) st_cluster_v2f64(cluster_map(at, j), v[u].x, v[u].y);
+                        } else {
+                            xd[2 * i] = v[u].x;
+                            if (2 * i + 1 < values) xd[2 * i + 1] = v[u].y;
+                        }
+                    }
                 }
             }
             __syncthreads();
-            // Release: the rows stored into `xd` before the barrier go with it.
-            if (tid == 0) store_release_gpu64(&relay->go, post_word(seq, rows));
-        } else {
-            for (int i = tid; i < values; i += kEngineThreads) xs[i] = __ldcg(xd + i);
+            if constexpr (CLUSTER) {
+                if (tid >= 1 && tid < blocks) {
+                    const uint32_t c = cluster_map(smem_u32(const_cast<unsigned int*>(ctl)), tid);
+                    st_cluster_u32(c, seq);
+                    st_cluster_u32(c + 4, cmd);
+                    st_cluster_u32(c + 8, static_cast<unsigned int>(rows));
+                    mbar_arrive_remote(cluster_map(smem_u32(rows_bar), tid));
+                }
+            } else if (tid == 0 && !cmd) {
+                // Release: the rows stored into `xd` before the barrier go with it.
+                store_release_gpu64(&relay->go, post_word(seq, rows));
+            }
+        } else if (!push) {
+            // Rows relayed through device memory: published by the release
+            // store (no cluster) or the cluster-scope arrival CTA 0 made
+            // after storing them.
+            if (!cmd) {
+                for (int i = tid; i < values; i += kEngineThreads) xs[i] = __ldcg(xd + i);
+            }
             __syncthreads();
         }
+        if (cmd) break;
         for (int i = tid; i < values; i += kEngineThreads) {
             const int f = i % a.F;
             put_keys<kEngineRows>(a, keys + i / a.F, slot_of[f], finish(a, xs[i], pre[2 * f], pre[2 * f + 1]),
@@ -280,16 +424,41 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         if (tid < rows) {
             double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
             for (int j = 0; j < nt; ++j) acc = __dadd_rn(acc, leafv[j * kEngineRows + tid]);
-            __stcg(bpart + static_cast<size_t>(block) * kEngineRows + tid, acc);
+            if constexpr (CLUSTER) {
+                st_cluster_f64(cluster_map(smem_u32(bsum + block * kEngineRows + tid), 0), acc);
+            } else {
+                __stcg(bpart + static_cast<size_t>(block) * kEngineRows + tid, acc);
+            }
         }
         __syncthreads();
-        if (tid == 0) {
-            const bool last = count_done(&relay->count) == blocks - 1;
-            if (last) relay->count = 0;  // every CTA has counted this request
-            ctl[1] = last;
+        bool last;
+        if constexpr (CLUSTER) {
+            if (tid == 0) mbar_arrive_remote(cluster_map(smem_u32(sum_bar), 0));
+            last = block == 0;
+            if (last) {
+                if (tid == 0) ctl[3] = mbar_wait_cluster(sum_bar, n & 1u, kEngineIdleNs) ? 1u : 0u;
+                __syncthreads();
+                if (!ctl[3]) {
+                    // A block never reported: tell every CTA to leave (the
+                    // host restarts the engine and the request stays posted).
+                    if (tid >= 1 && tid < blocks) {
+                        const uint32_t c = cluster_map(smem_u32(const_cast<unsigned int*>(ctl)), tid);
+                        st_cluster_u32(c + 4, 1u);
+                        mbar_arrive_remote(cluster_map(smem_u32(rows_bar), tid));
+                    }
+                    break;
+                }
+            }
+        } else {
+            if (tid == 0) {
+                const bool is_last = count_done(&relay->count) == blocks - 1;
+                if (is_last) relay->count = 0;  // every CTA has counted this request
+                ctl[1] = is_last;
+            }
+            __syncthreads();
+            last = ctl[1] != 0;
         }
-        __syncthreads();
-        if (ctl[1]) {
+        if (last) {
             if (tid < rows) {
                 // The block sums, 16 loads in flight at a time, added in
                 // block order.
@@ -299,7 +468,11 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
                     double t[kBatch];
 #pragma unroll
                     for (int j = 0; j < kBatch; ++j) {
-                        t[j] = b0 + j < blocks ? __ldcg(bpart + static_cast<size_t>(b0 + j) * kEngineRows + tid) : 0.0;
+                        if constexpr (CLUSTER) {
+                            t[j] = b0 + j < blocks ? bsum[(b0 + j) * kEngineRows + tid] : 0.0;
+                        } else {
+                            t[j] = b0 + j < blocks ? __ldcg(bpart + static_cast<size_t>(b0 + j) * kEngineRows + tid) : 0.0;
+                        }
                     }
 #pragma unroll
                     for (int j = 0; j < kBatch; ++j) {
@@ -307,8 +480,8 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
                     }
                 }
                 if (a.mean) {
-                    const int n = __ldg(a.counts);
-                    v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
+                    const int c = __ldg(a.counts);
+                    v[0] = __dadd_rn(__ldg(a.base), c ? __ddiv_rn(v[0], static_cast<double>(c)) : 0.0);
                 }
                 apply_link<1>(a, v, 1);
                 const unsigned long long tag = seq;
@@ -318,25 +491,28 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             }
         }
         mine = seq;
-        __syncthreads();  // every thread has read this request's control words before thread 0 rewrites them
+        ++n;
+        __syncthreads();  // every thread has read this request's control words before they are rewritten
     }
+    if constexpr (CLUSTER) cluster_sync();
 }
 
 template <int D, bool LEAF32>
-void* engine_of() {
-    return reinterpret_cast<void*>(&engine_kernel<D, LEAF32>);
+void* engine_of(bool cluster) {
+    return cluster ? reinterpret_cast<void*>(&engine_kernel<D, LEAF32, true>)
+                   : reinterpret_cast<void*>(&engine_kernel<D, LEAF32, false>);
 }
 
-void* pick_engine(int depth, bool leaf32) {
+void* pick_engine(int depth, bool leaf32, bool cluster) {
     switch (depth) {
-        case 1: return leaf32 ? engine_of<1, true>() : engine_of<1, false>();
-        case 2: return leaf32 ? engine_of<2, true>() : engine_of<2, false>();
-        case 3: return leaf32 ? engine_of<3, true>() : engine_of<3, false>();
-        case 4: return leaf32 ? engine_of<4, true>() : engine_of<4, false>();
-        case 5: return leaf32 ? engine_of<5, true>() : engine_of<5, false>();
-        case 6: return leaf32 ? engine_of<6, true>() : engine_of<6, false>();
-        case 7: return leaf32 ? engine_of<7, true>() : engine_of<7, false>();
-        case 8: return leaf32 ? engine_of<8, true>() : engine_of<8, false>();
+        case 1: return leaf32 ? engine_of<1, true>(cluster) : engine_of<1, false>(cluster);
+        case 2: return leaf32 ? engine_of<2, true>(cluster) : engine_of<2, false>(cluster);
+        case 3: return leaf32 ? engine_of<3, true>(cluster) : engine_of<3, false>(cluster);
+        case 4: return leaf32 ? engine_of<4, true>(cluster) : engine_of<4, false>(cluster);
+        case 5: return leaf32 ? engine_of<5, true>(cluster) : engine_of<5, false>(cluster);
+        case 6: return leaf32 ? engine_of<6, true>(cluster) : engine_of<6, false>(cluster);
+        case 7: return leaf32 ? engine_of<7, true>(cluster) : engine_of<7, false>(cluster);
+        case 8: return leaf32 ? engine_of<8, true>(cluster) : engine_of<8, false>(cluster);
     }
     return nullptr;
 }
@@ -365,6 +541,7 @@ struct LatencyEngine {
     void* dev = nullptr;            // block sums, relayed rows, then the Relay words
     unsigned int seq = 0;
     bool launched = false;
+    bool cluster = false;  // running as one thread-block cluster
 
     Mailbox* box() const { return reinterpret_cast<Mailbox*>(host); }
     double* x_host() const { return reinterpret_cast<double*>(host + 64); }
@@ -392,11 +569,37 @@ bool engine_fits(const DevForest& f, long long batch) {
 
 // Starts (or restarts) the engine of `e` for forest `f`; `first` is the
 // request number the engine treats as already answered.
+// An engine of at most kClusterBlocks blocks runs as one thread-block
+// cluster when the GPU can place it; otherwise as a cooperative launch.
 static bool engine_launch(const DevForest& f, LatencyEngine& e, unsigned int first, std::string& err) {
-    void* k = pick_engine(f.heap.depth, f.heap.leaf32 != 0);
     const int smem = engine_smem(f.args.slots, f.args.F, heap_record_bytes(f.heap.depth, f.heap.leaf32));
-    if (!k || !checked(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                       "cudaFuncSetAttribute", err)) {
+    bool cluster = e.blocks <= kClusterBlocks;
+    void* kc = pick_engine(f.heap.depth, f.heap.leaf32 != 0, true);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    if (cluster && kc) {
+        cfg.gridDim = dim3(static_cast<unsigned>(e.blocks));
+        cfg.blockDim = dim3(kEngineThreads);
+        cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+        cfg.stream = e.stream;
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(e.blocks);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        cluster = cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+                  (e.blocks <= 8 ||
+                   cudaFuncSetAttribute(kc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) &&
+                  cudaOccupancyMaxActiveClusters(&clusters, kc, &cfg) == cudaSuccess && clusters >= 1;
+        cudaGetLastError();
+    } else {
+        cluster = false;
+    }
+    void* k = cluster ? kc : pick_engine(f.heap.depth, f.heap.leaf32 != 0, false);
+    if (!k || (!cluster && !checked(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                                    "cudaFuncSetAttribute", err))) {
         if (!k) err = "no latency engine for this model";
         return false;
     }
@@ -417,11 +620,11 @@ static bool engine_launch(const DevForest& f, LatencyEngine& e, unsigned int fir
     ForestArgs a = f.args;
     HeapArgs h = f.heap;
     void* args[] = {&a, &h, &box, &x, &out, &bpart, &xd, &relay, &first};
-    if (!checked(cudaLaunchCooperativeKernel(k, e.blocks, kEngineThreads, args, smem, e.stream),
-                 "latency engine launch", err)) {
-        return false;
-    }
+    const cudaError_t launched = cluster ? cudaLaunchKernelExC(&cfg, k, args)
+                                         : cudaLaunchCooperativeKernel(k, e.blocks, kEngineThreads, args, smem, e.stream);
+    if (!checked(launched, "latency engine launch", err)) return false;
     e.launched = true;
+    e.cluster = cluster;
     return true;
 }
 

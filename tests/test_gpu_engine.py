@@ -4,7 +4,11 @@ With latency threads on (montlok_set_latency_threads(n > 0), the setting the
 reference uses for its spinning single-row workers), host-buffer predicts of
 at most 8 rows on complete-tree models go to a kernel that stays resident per
 calling thread, holds each 64-tree block in one CTA's shared memory and
-answers requests posted in pinned host memory. Every answer must carry the
+answers requests posted in pinned host memory. Engines of at most 16 blocks
+run as one thread-block cluster (rows pushed into every CTA's shared memory
+for requests of 1 or 2 c5 rows, relayed through device memory for larger
+ones; block sums gathered in CTA 0's shared memory); larger ones meet through
+device memory (the 1100-tree model, 18 blocks). Every answer must carry the
 oracle's bits: preprocessing, float32 and float64 models (ties decided on the
 double), every missing-value rule, mean aggregation, float32 inputs, every
 row count up to 8, several threads each with their own engine, an engine that
@@ -42,10 +46,11 @@ def models():
         "f64_every_rule": random_model(rng, features=7, trees=150, max_depth=8, inf_thresholds=0.1, link="sigmoid"),
         "f32_lt_mean": random_model(rng, features=6, trees=70, max_depth=6, cast="f32", decision="lt",
                                     aggregate="mean", base=0.5),
+        "blocks_18": random_model(rng, features=10, trees=1100, max_depth=6, inf_thresholds=0.05, link="sigmoid"),
     }
 
 
-@pytest.mark.parametrize("name", ["c5", "f64_every_rule", "f32_lt_mean"])
+@pytest.mark.parametrize("name", ["c5", "f64_every_rule", "f32_lt_mean", "blocks_18"])
 def test_engine_answers_small_calls_exactly(engine, name):
     model = models()[name]
     m, o = montlok.load(model), Oracle(model)
