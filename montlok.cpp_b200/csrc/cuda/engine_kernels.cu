@@ -10,23 +10,30 @@
 // eight shared loads. The calling thread writes the request's rows into a
 // mailbox in pinned host memory and posts its number and row count in one
 // 64-bit word. Thread 0 of CTA 0 polls that word (system-scope acquire loads;
-// the only poller of the bus), CTA 0 reads the rows over the bus in 16-byte
-// loads and relays them through device memory, publishing the word in device
-// memory (a release store the other CTAs poll with acquire loads). Every CTA then builds the rows' keys, walks its 64 trees
-// for each row (one thread per tree and row pair) and adds the leaves in tree
-// order into its block's partial sum. The last CTA to finish (a device-scope
-// acquire-release counter, no waiting) loads the block sums sixteen at a time
-// and adds them in block order, applies the link
-// and writes each row's answer into the mailbox as one 16-byte record with
-// the request's number; the caller spins on those numbers.
+// the only poller of the bus) and CTA 0 reads the rows over the bus in 16-byte
+// loads. Engines of at most kClusterBlocks blocks run as one thread-block
+// cluster: CTA 0 pushes the rows into every CTA's shared memory (or, for
+// large requests, through device memory) and wakes each CTA with a remote
+// mbarrier arrival; every CTA builds the rows' keys, walks its 64 trees for
+// each row (one thread per tree and row pair), adds the leaves in tree order
+// and pushes its block sum into CTA 0's shared memory, arriving on CTA 0's
+// barrier; CTA 0 adds the block sums in block order and applies the link.
+// Larger engines are a cooperative launch whose CTAs meet through device
+// memory: CTA 0 relays the rows and publishes the post word with a release
+// store the others poll; the last CTA to finish (an acquire-release counter,
+// no waiting) loads the block sums sixteen at a time and adds them in order.
+// Either way each row's answer is written into the mailbox as one 16-byte
+// record with the request's number; the caller spins on those numbers.
 //
 // Every wait is bounded. An engine CTA exits when the host asks (stop), when
-// CTA 0 has seen no request for kEngineIdleNs (it raises a quit flag the
-// others follow; they also leave after twice that) or after kEnginePolls
-// polls. The host starts the engine on
-// demand with a cooperative launch (all CTAs resident, or the launch fails
-// and the call takes the graph path), relaunches it when it has exited, and
-// gives up on a request after kEngineTimeoutNs with MONTLOK_ERROR_INTERNAL.
+// CTA 0 has seen no request for kEngineIdleNs (it tells the others: a quit
+// flag, or in the cluster a pushed order to leave; they also leave on their
+// own after a longer wait) or after kEnginePolls polls; the cluster form's
+// CTAs leave through a cluster barrier. The host starts the engine on demand
+// (a cluster launch when the GPU can place it, else a cooperative launch; if
+// neither can start the call takes the graph path), relaunches it when it has
+// exited, and gives up on a request after kEngineTimeoutNs with
+// MONTLOK_ERROR_INTERNAL.
 #include <atomic>
 #include <chrono>
 #include <cstring>
