@@ -47,10 +47,11 @@ def models():
         "f32_lt_mean": random_model(rng, features=6, trees=70, max_depth=6, cast="f32", decision="lt",
                                     aggregate="mean", base=0.5),
         "blocks_18": random_model(rng, features=10, trees=1100, max_depth=6, inf_thresholds=0.05, link="sigmoid"),
+        "one_block": random_model(rng, features=5, trees=40, max_depth=7, link="exp"),  # a cluster of one CTA
     }
 
 
-@pytest.mark.parametrize("name", ["c5", "f64_every_rule", "f32_lt_mean", "blocks_18"])
+@pytest.mark.parametrize("name", ["c5", "f64_every_rule", "f32_lt_mean", "blocks_18", "one_block"])
 def test_engine_answers_small_calls_exactly(engine, name):
     model = models()[name]
     m, o = montlok.load(model), Oracle(model)
