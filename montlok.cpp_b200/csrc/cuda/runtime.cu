@@ -1164,6 +1164,43 @@ void mlk_cuda_forest_release(mlk_dev_forest* forest) {
     delete forest;
 }
 
+namespace {
+
+// The device-buffer calls' scratch comes from a memory pool of the library's
+// own per device, which keeps up to kPoolKeep bytes mapped across
+// synchronisations (the default pool returns its memory at every
+// synchronisation, so a caller that synchronises after each small call would
+// pay a fresh mapping per call). Null when the pool cannot be made: calls then
+// use the default pool.
+constexpr uint64_t kPoolKeep = uint64_t{256} << 20;
+
+cudaMemPool_t scratch_pool(int device) {
+    static std::mutex mu;
+    static std::map<int, cudaMemPool_t> pools;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = pools.find(device);
+    if (it != pools.end()) return it->second;
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) == cudaSuccess) {
+        uint64_t keep = kPoolKeep;
+        if (cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess) {
+            cudaMemPoolDestroy(pool);
+            pool = nullptr;
+        }
+    } else {
+        pool = nullptr;
+    }
+    cudaGetLastError();
+    pools[device] = pool;
+    return pool;
+}
+
+}  // namespace
+
 static int device_call(const mlk_dev_forest* forest, int dtype, const void* x, size_t batch, double* out,
                        int32_t* leaves, void* stream, char* err, size_t errlen) {
     using namespace mlk::cuda;
@@ -1173,9 +1210,13 @@ static int device_call(const mlk_dev_forest* forest, int dtype, const void* x, s
     const size_t scratch = scratch_bytes(forest->f, static_cast<long long>(batch));
     void* tmp = nullptr;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (scratch && !ok(cudaMallocAsync(&tmp, scratch, st), "cudaMallocAsync", e)) {
-        put_error(err, errlen, e);
-        return kInternal;
+    if (scratch) {
+        cudaMemPool_t pool = scratch_pool(forest->f.device);
+        const cudaError_t a = pool ? cudaMallocFromPoolAsync(&tmp, scratch, pool, st) : cudaMallocAsync(&tmp, scratch, st);
+        if (!ok(a, "cudaMallocAsync", e)) {
+            put_error(err, errlen, e);
+            return kInternal;
+        }
     }
     bool good = true;
     if (injected("launch")) {
