@@ -42,6 +42,7 @@
 #include <thread>
 
 #include "async_copy.cuh"
+#include "cluster.cuh"
 #include "device_common.cuh"
 #include "engine.cuh"
 #include "forest.cuh"
@@ -152,23 +153,6 @@ __device__ __forceinline__ int count_done(int* p) {
     return old;
 }
 
-// Distributed shared memory of a thread-block cluster (the engine's cluster
-// form): the address of a shared variable in CTA `rank`, stores into it, and
-// remote mbarrier arrivals.
-__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
-    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_f64(uint32_t addr, double v) {
-    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_v2f64(uint32_t addr, double v0, double v1) {
-    asm volatile("st.shared::cluster.v2.f64 [%0], {%1, %2};" ::"r"(addr), "d"(v0), "d"(v1) : "memory");
-}
 // Release at cluster scope: the CTA's stores before its barrier reach the
 // waiter with the arrival.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
@@ -193,10 +177,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         if (global_ns() - t0 > limit_ns) return false;
     }
     return false;
-}
-// Every thread of every CTA of the cluster.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // CLUSTER: the engine's CTAs form one thread-block cluster (at most

@@ -125,6 +125,9 @@ int heap_slot_bits(int slots);
 // latency_scratch_bytes(f) bytes).
 size_t latency_scratch_bytes(const DevForest& f);
 bool latency_fits(const DevForest& f, long long batch);
+// 0: the counter form; 1, 2: the cluster form (2: CTA 0 reads the rows once,
+// so they may be in pinned host memory).
+int latency_form(const DevForest& f, int dtype, long long batch);
 bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                     std::string& err, void* scratch, int* counters);
 bool launch_heap(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,

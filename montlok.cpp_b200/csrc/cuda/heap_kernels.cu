@@ -51,6 +51,7 @@
 #include "device_common.cuh"
 #include "forest.cuh"
 #include "tmem.cuh"
+#include "cluster.cuh"
 
 namespace mlk::cuda {
 namespace {
@@ -790,6 +791,150 @@ __global__ void __launch_bounds__(kLatencyThreads) latency_kernel(const __grid_c
     out[row] = v[0];
 }
 
+
+// ---------------------------------------------------------------------------
+// Cluster form of the small-batch kernel, for forests of at most
+// kClusterBlocks 64-tree blocks: the CTAs of one row group (one per block)
+// form a thread-block cluster. CTA 0 of the cluster reads the group's rows
+// once (uncached: in the host-call path they are read straight from the
+// pinned staging buffer, so the call's graph has no copy node) and pushes
+// them into every CTA's shared memory; after a cluster barrier each CTA
+// builds the keys, walks its 64 trees as latency_kernel does and pushes its
+// block sum into CTA 0's shared memory; after a second barrier CTA 0 adds the
+// block sums in block order, applies the link and stores the rows' results.
+// No device scratch, counter or fence. Requests whose copies would total more
+// than kClusterPush values let every CTA read the rows itself instead.
+// ---------------------------------------------------------------------------
+constexpr int kClusterBlocks = 16;
+constexpr int kClusterPush = 6144;
+
+__device__ __forceinline__ double load_uncached(const double* p) {
+    double v;
+    asm volatile("ld.global.cv.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ double load_uncached(const float* p) {
+    float v;
+    asm volatile("ld.global.cv.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return static_cast<double>(v);
+}
+
+// Shared memory: pad | keys [slot][row] | leaf values [tree][row] | rows
+// [row][F] (doubles) | block sums [block][row] (used in CTA 0).
+__host__ __device__ inline int latency_cluster_smem(int slots, int F) {
+    return 128 + align128(slots * kGroupRows * 4) + kTreeBlock * kGroupRows * 8 + align128(kGroupRows * F * 8) +
+           kClusterBlocks * kGroupRows * 8;
+}
+
+template <int D, bool LEAF32, typename XT>
+__global__ void __launch_bounds__(kLatencyThreads) latency_cluster_kernel(const __grid_constant__ ForestArgs a,
+                                                                          const __grid_constant__ HeapArgs h,
+                                                                          const XT* __restrict__ x, long long batch,
+                                                                          double* __restrict__ out) {
+    constexpr int kRec = record_bytes(D, LEAF32);
+    constexpr int kSplits = (1 << D) - 1;
+    extern __shared__ __align__(128) unsigned char smem[];
+    int* keys = reinterpret_cast<int*>(smem + 128);  // [slot][kGroupRows]
+    double* leafv = reinterpret_cast<double*>(smem + 128 + align128(a.slots * kGroupRows * 4));  // [tree][row]
+    double* xs = leafv + kTreeBlock * kGroupRows;                                                 // [row][F]
+    double* bsum = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(xs) + align128(kGroupRows * a.F * 8));
+
+    const int tid = threadIdx.x;
+    const int blocks = (a.T + kTreeBlock - 1) / kTreeBlock;  // the cluster's size
+    const int block = blockIdx.x % blocks, group = blockIdx.x / blocks;
+    const long long row0 = static_cast<long long>(kGroupRows) * group;
+    const int rows = static_cast<int>(min(static_cast<long long>(kGroupRows), batch - row0));
+    const int t0 = block * kTreeBlock;
+    const int nt = min(kTreeBlock, a.T - t0);
+    const uint32_t mask = (1u << h.slot_bits) - 1u;
+    const int values = rows * a.F;
+    const XT* xr = x + row0 * a.F;
+
+    if (values * (blocks - 1) <= kClusterPush) {
+        if (block == 0) {
+            for (int i = tid; i < values; i += kLatencyThreads) {
+                const double v = load_uncached(xr + i);
+                xs[i] = v;
+                const uint32_t at = smem_u32(xs + i);
+                for (int j = 1; j < blocks; ++j) st_cluster_f64(cluster_map(at, j), v);
+            }
+        }
+    } else {
+        for (int i = tid; i < values; i += kLatencyThreads) xs[i] = load_x(xr + i);
+    }
+    cluster_sync();  // the rows are in every CTA
+
+    for (int i = tid; i < values; i += kLatencyThreads) {
+        const int f = i % a.F;
+        const double mean = a.standardize ? __ldg(a.pre_mean + f) : 0.0;
+        const double scale = a.standardize ? __ldg(a.pre_scale + f) : 1.0;
+        put_keys<kGroupRows>(a, keys + i / a.F, __ldg(a.slot_of + f), finish(a, xs[i], mean, scale),
+                             static_cast<int>(mask));
+    }
+    if (tid < kGroupRows) keys[a.pad_slot * kGroupRows + tid] = INT_MIN;
+    __syncthreads();
+
+    // Walks: thread (pair, lane) takes tree t0 + tid % 64 for rows pair and
+    // pair + 4 of the group, reading the L2-resident records.
+    const int local = tid % kTreeBlock, pair = tid / kTreeBlock;
+    const int tree = t0 + local;
+    if (local < nt && pair < rows) {
+        const unsigned char* rec = h.trees + static_cast<size_t>(tree) * kRec;
+        const int ra = pair, rb = pair + kRowPairs;
+        const bool two = rb < rows;
+        const int* ca = keys + ra;
+        const int* cb = keys + rb;
+        uint32_t ia = 0, ib = 0;
+        bool tie = false;
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            const uint32_t na = split_word(rec, ia);
+            const uint32_t nb = split_word(rec, ib);
+            const int ka = ca[(na & mask) * kGroupRows];
+            const int kb = cb[(nb & mask) * kGroupRows];
+            tie |= ka == static_cast<int>(na) || (two && kb == static_cast<int>(nb));
+            ia = 2 * ia + (ka > static_cast<int>(na) ? 2u : 1u);
+            ib = 2 * ib + (kb > static_cast<int>(nb) ? 2u : 1u);
+        }
+        if (tie) {
+            ia = walk_global<D>(a, h, rec, ca, mask, tree, x, row0 + ra, batch, true);
+            if (two) ib = walk_global<D>(a, h, rec, cb, mask, tree, x, row0 + rb, batch, true);
+        }
+        auto leaf = [&](uint32_t i) {
+            const unsigned char* at = rec + (4 << D);
+            const uint32_t l = i - kSplits;
+            return LEAF32 ? static_cast<double>(__ldg(reinterpret_cast<const float*>(at) + l))
+                          : __ldg(reinterpret_cast<const double*>(at) + l);
+        };
+        leafv[local * kGroupRows + ra] = leaf(ia);
+        if (two) leafv[local * kGroupRows + rb] = leaf(ib);
+    }
+    __syncthreads();
+    if (tid < rows) {
+        double acc = (block == 0 && !a.mean) ? __ldg(a.base) : 0.0;
+        for (int j0 = 0; j0 < nt; j0 += 8) {
+            double v[8];  // the loads together, the adds in order
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = j0 + j < nt ? leafv[(j0 + j) * kGroupRows + tid] : 0.0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (j0 + j < nt) acc = __dadd_rn(acc, v[j]);
+            }
+        }
+        st_cluster_f64(cluster_map(smem_u32(bsum + block * kGroupRows + tid), 0), acc);
+    }
+    cluster_sync();  // every block sum is in CTA 0
+    if (block != 0 || tid >= rows) return;
+    double v[1] = {bsum[tid]};
+    for (int b = 1; b < blocks; ++b) v[0] = __dadd_rn(v[0], bsum[b * kGroupRows + tid]);
+    if (a.mean) {
+        const int n = __ldg(a.counts);
+        v[0] = __dadd_rn(__ldg(a.base), n ? __ddiv_rn(v[0], static_cast<double>(n)) : 0.0);
+    }
+    apply_link<1>(a, v, 1);
+    out[row0 + tid] = v[0];
+}
+
 template <int D, bool LEAF32, typename XT>
 void* latency_of() {
     return reinterpret_cast<void*>(&latency_kernel<D, LEAF32, XT>);
@@ -799,6 +944,30 @@ template <int D>
 void* pick_latency_leaf(bool leaf32, bool f64) {
     if (leaf32) return f64 ? latency_of<D, true, double>() : latency_of<D, true, float>();
     return f64 ? latency_of<D, false, double>() : latency_of<D, false, float>();
+}
+
+template <int D>
+void* pick_latency_cluster_leaf(bool leaf32, bool f64) {
+    if (leaf32) {
+        return f64 ? reinterpret_cast<void*>(&latency_cluster_kernel<D, true, double>)
+                   : reinterpret_cast<void*>(&latency_cluster_kernel<D, true, float>);
+    }
+    return f64 ? reinterpret_cast<void*>(&latency_cluster_kernel<D, false, double>)
+               : reinterpret_cast<void*>(&latency_cluster_kernel<D, false, float>);
+}
+
+void* pick_latency_cluster(int depth, bool leaf32, bool f64) {
+    switch (depth) {
+        case 1: return pick_latency_cluster_leaf<1>(leaf32, f64);
+        case 2: return pick_latency_cluster_leaf<2>(leaf32, f64);
+        case 3: return pick_latency_cluster_leaf<3>(leaf32, f64);
+        case 4: return pick_latency_cluster_leaf<4>(leaf32, f64);
+        case 5: return pick_latency_cluster_leaf<5>(leaf32, f64);
+        case 6: return pick_latency_cluster_leaf<6>(leaf32, f64);
+        case 7: return pick_latency_cluster_leaf<7>(leaf32, f64);
+        case 8: return pick_latency_cluster_leaf<8>(leaf32, f64);
+    }
+    return nullptr;
 }
 
 void* pick_latency(int depth, bool leaf32, bool f64) {
@@ -980,9 +1149,91 @@ bool latency_fits(const DevForest& f, long long batch) {
     return latency_smem(f.args.slots, h.depth, h.leaf32) <= kHeapSmemLimit;
 }
 
+// Which form of the small-batch kernel a call of `batch` rows runs: 0 the
+// counter form (latency_kernel), 1 the cluster form with every CTA reading
+// the rows, 2 the cluster form with CTA 0 reading them once (the rows may
+// then sit in pinned host memory). The cluster form needs at most
+// kClusterBlocks blocks and a GPU that can place such a cluster (checked once
+// per kernel and device).
+int latency_form(const DevForest& f, int dtype, long long batch) {
+    const HeapArgs& h = f.heap;
+    const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
+    if (!latency_fits(f, batch) || blocks > kClusterBlocks) return 0;
+    const int smem = latency_cluster_smem(f.args.slots, f.args.F);
+    if (smem > kHeapSmemLimit) return 0;
+    void* k = pick_latency_cluster(h.depth, h.leaf32, dtype == 2);
+    if (!k) return 0;
+    // (kernel, device, cluster size, shared memory) -> whether the GPU can place it
+    struct Known {
+        void* kernel;
+        int device, blocks, smem;
+        bool can;
+    };
+    static std::mutex mu;
+    static std::vector<Known> known;
+    bool can = false;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = std::find_if(known.begin(), known.end(), [&](const Known& e) {
+            return e.kernel == k && e.device == f.device && e.blocks == blocks && e.smem == smem;
+        });
+        if (it != known.end()) {
+            can = it->can;
+        } else {
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr[1];
+            cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+            cfg.blockDim = dim3(kLatencyThreads);
+            cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(blocks);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            can = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeapSmemLimit) == cudaSuccess &&
+                  (blocks <= 8 ||
+                   cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) &&
+                  cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) == cudaSuccess && clusters >= 1;
+            cudaGetLastError();
+            known.push_back(Known{k, f.device, blocks, smem, can});
+        }
+    }
+    if (!can) return 0;
+    const long long rows = std::min<long long>(batch, kGroupRows);
+    return rows * f.args.F * (blocks - 1) <= kClusterPush ? 2 : 1;
+}
+
 bool launch_latency(const DevForest& f, int dtype, const void* x, long long batch, double* out, cudaStream_t stream,
                     std::string& err, void* scratch, int* counters) {
     const HeapArgs& h = f.heap;
+    if (latency_form(f, dtype, batch) > 0) {
+        void* k = pick_latency_cluster(h.depth, h.leaf32, dtype == 2);
+        const int blocks = (f.args.T + kTreeBlock - 1) / kTreeBlock;
+        const int groups = static_cast<int>((batch + kGroupRows - 1) / kGroupRows);
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        cfg.gridDim = dim3(static_cast<unsigned>(blocks * groups));
+        cfg.blockDim = dim3(kLatencyThreads);
+        cfg.dynamicSmemBytes = static_cast<size_t>(latency_cluster_smem(f.args.slots, f.args.F));
+        cfg.stream = stream;
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(blocks);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        ForestArgs a = f.args;
+        HeapArgs hh = h;
+        void* args[] = {&a, &hh, const_cast<void**>(&x), &batch, &out};
+        const cudaError_t e = cudaLaunchKernelExC(&cfg, k, args);
+        if (e != cudaSuccess) {
+            err = std::string("small-batch kernel launch: ") + cudaGetErrorString(e);
+            return false;
+        }
+        return true;
+    }
     void* k = pick_latency(h.depth, h.leaf32, dtype == 2);
     if (!k) {
         err = "no small-batch complete-tree kernel for this model";

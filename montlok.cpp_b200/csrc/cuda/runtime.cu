@@ -349,15 +349,15 @@ constexpr size_t kGraphCache = 8;    // graphs kept per workspace
 // input is pinned already, the graph's copy reads it in place), a cached
 // graph of (host -> device copy, kernel) runs on the workspace's first
 // stream, the kernel storing its results into pinned host memory directly,
-// and the result is copied out. (Calls of at most kDirectRows rows could skip
-// the device copy, the kernel reading the staged rows over the bus; measured
-// slower for 1 and 8 rows, 21.5 and 30.6 us against 18.1 and 22.1, since
-// every CTA pays the bus latency, so it is off.) The graph is captured
-// on the first call with this forest, input type and row count (or after a
-// staging buffer grew), so later calls of the same shape pay one graph
-// launch instead of separate stream operations and kernel launches.
-constexpr size_t kDirectRows = 0;  // small-batch calls whose kernel reads the rows from pinned host memory
-
+// and the result is copied out. When the small-batch kernel runs in its
+// cluster form with one CTA reading the rows (latency_form 2), the kernel
+// reads them straight from the pinned staging buffer and the graph is one
+// kernel node. (The counter form reading them over the bus from every CTA
+// was slower than the copy: 21.5 and 30.6 us against 18.1 and 22.1 for 1 and
+// 8 rows.) The graph is captured on the first call with this forest, input
+// type and row count (or after a staging buffer grew), so later calls of the
+// same shape pay one graph launch instead of separate stream operations and
+// kernel launches.
 int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_t batch, double* out, char* err,
               size_t errlen) {
     std::string e;
@@ -380,9 +380,9 @@ int run_small(const DevForest& base, int dtype, const void* x, int x_kind, size_
         return kInternal;
     }
     cudaStream_t st = w->stream[0];
-    // The fewest rows need no copy at all: the kernel reads them from the
-    // pinned staging buffer over the bus, so the graph is one kernel node.
-    const bool direct = batch <= kDirectRows && latency_fits(f, static_cast<long long>(batch));
+    // No copy when the kernel's first CTA reads the rows from the pinned
+    // staging buffer over the bus: the graph is one kernel node.
+    const bool direct = latency_form(f, dtype, static_cast<long long>(batch)) == 2;
     const void* kernel_x = direct ? w->hx[0].p : w->dx[0].p;
     const void* buffers[5] = {w->dx[0].p, nullptr, w->hx[0].p, w->hout[0].p, scratch ? w->scratch.p : nullptr};
     CachedGraph* g = nullptr;

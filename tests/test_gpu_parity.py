@@ -349,9 +349,11 @@ def test_stream_is_stateless_predict(gpu):
 
 @pytest.mark.parametrize("fault", ["alloc", "copy", "launch"])
 def test_injected_cuda_failures_are_clean_errors(gpu, fault):
+    # 100 rows: past the small-batch kernel, whose cluster form reads small
+    # calls' rows from pinned memory with no copy for "copy" to fail
     rng = np.random.default_rng(9)
     m = montlok.load(random_model(rng, features=4, trees=10))
-    x = edge_inputs(rng, 50, 4)
+    x = edge_inputs(rng, 100, 4)
     expected = m.predict(x)
     errors = []
 
